@@ -1,0 +1,151 @@
+/*
+ * mimizuku_b200: the B200-native (sm_100a) attention hot path of the mimizuku Whisper engine, as a C-ABI library.
+ *
+ * Conventions
+ *   - Device buffers are plain CUDA device pointers; fp16 tensors are IEEE binary16 (`uint16_t` bit patterns on the
+ *     host side). Layouts are the reference engine's (paths below are inside the hayatree/mimizuku project).
+ *   - `stream` is a cudaStream_t / CUstream (NULL = legacy default stream). Kernel entry points are asynchronous and
+ *     never allocate, so they may be captured in a CUDA graph; call mmz_init on the device first.
+ *   - Every function returns 0 on success and a negative value on error; mmz_last_error() then describes the error
+ *     (thread-local). Asynchronous kernel faults surface at the next synchronisation, as in the reference
+ *     (src/gpu.rs:187-201 checks only the launch).
+ *   - In-kernel waits are bounded; a wait that gives up records a code in the device status word (mmz_status).
+ */
+#ifndef MIMIZUKU_B200_H
+#define MIMIZUKU_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- library */
+
+/* Initialises the library on `device` and makes it current (status word, kernel attributes). Replaces the set-up
+ * part of Gpu::new (src/gpu.rs:122-137). */
+int mmz_init(int device);
+const char* mmz_last_error(void);
+/* Reads and clears the device status word of the current device: code[0] error (0 none, 1 wait timed out,
+ * 2 misaligned shared memory, 3 bad argument), code[1] kernel (1 enc_flash, 2 self_attn, 3 cross_attn), code[2] site.
+ * Synchronises the device. No reference counterpart (the reference has no in-kernel failure detection). */
+int mmz_status(int code[3]);
+/* Sets the bound on every in-kernel wait, in milliseconds (default 1000). */
+int mmz_set_wait_limit_ms(int device, int ms);
+
+/* ---------------------------------------------------------------- fp16 helpers (src/gpu.rs:79-119) */
+
+float mmz_h2f(uint16_t h);      /* src/gpu.rs:79-91 */
+uint16_t mmz_f2h(float x);      /* src/gpu.rs:93-114, round to nearest even */
+float mmz_rh(float x);          /* src/gpu.rs:116-119 */
+
+/* ---------------------------------------------------------------- attention hot path (device pointers) */
+
+/* Encoder self-attention, non-causal, over the 1500 encoder positions of `groups` clips:
+ * qkv [groups][1500][3d] fp16 (Q at column h*64, K at d + h*64, V at 2d + h*64), out [groups][1500][d] fp16.
+ * tcgen05 / TMEM / TMA flash attention. Replaces the enc_flash launch (kernels/whisper.cu:209,
+ * src/model.rs:566: grid (24, heads, groups), block 128). qkv and out 16-byte aligned. */
+int mmz_enc_flash(const void* qkv, void* out, int groups, int d, void* stream);
+
+/* Causal decoder self-attention at position p = ctr[0] over the per-layer caches kc, vc [batch][max_t][d], with the
+ * cache write of position p folded in: k and v of p are read from qkv [batch][3d] and stored into the caches.
+ * Sequences with done[b] != 0 only get the cache write. out [batch][d]. Replaces kv_write + self_attn
+ * (kernels/whisper.cu:310, :321; src/model.rs:665-672). max_t <= 512. */
+int mmz_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* ctr, const int* done, int batch,
+                  int max_t, int d, void* stream);
+
+/* kv_write alone (kernels/whisper.cu:310; src/model.rs:665): k, v of position ctr[0] from qkv into the caches. */
+int mmz_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch, int max_t, int d, void* stream);
+
+/* Decoder cross-attention of one layer over the 1500 encoder positions: q [batch][d] (the xq projection), kv the
+ * head-contiguous cross k/v buffer [batch][nl][k|v][heads][1500][64], out [batch][d]. For the heads with
+ * aslot[layer * heads + head] = s >= 0, the fp16 probabilities are also stored into align[b][ctr[0]][s][1500]
+ * (align is [batch][max_t][na][1500]). Sequences with done[b] != 0 are skipped. One fused launch replaces
+ * cross_scores + cross_pv + cross_combine (kernels/whisper.cu:368, :407, :443; src/model.rs:676-705) and needs none
+ * of their S / stat / part scratch. kv 16-byte aligned. */
+int mmz_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
+                   const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* stream);
+
+/* out = layernorm(x) per row of `dim` (even, <= 2048) fp16 values, fp32 statistics, eps as given.
+ * Replaces layernorm (kernels/whisper.cu:66; src/model.rs:529-531). */
+int mmz_layernorm(const void* x, const void* w, const void* b, void* out, int rows, int dim, float eps, void* stream);
+/* x = h(x + d) in place, then out = layernorm(x); out may be d. Replaces add_layernorm (kernels/whisper.cu:72;
+ * src/model.rs:533-537). */
+int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
+                      void* stream);
+
+/* ---------------------------------------------------------------- token timestamps (host, src/align.rs) */
+
+/* w [rows][heads][cols_full] alignment-head probabilities -> out [rows] start times in seconds (cols = audio frames
+ * / 2, width = median filter width, 7 in the reference). src/align.rs:8-63. */
+int mmz_jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out);
+/* DTW over cost m [rows][cols]; writes the path into text, time (rows + cols entries each) and its length into
+ * *len. src/align.rs:66-106. */
+int mmz_dtw(const double* m, int rows, int cols, int* text, int* time, int* len);
+
+/* ---------------------------------------------------------------- features (host, src/audio.rs) */
+
+/* Log-mel [n_mels][3000] of the first 30 s of 16 kHz samples y[n]; *frames = 10 ms frames that hold audio.
+ * src/audio.rs:192-237. */
+int mmz_log_mel(const float* y, long n, int n_mels, float* out, int* frames);
+/* The same for `count` clips on `threads` host threads (src/transcribe.rs:25-56); out [count][n_mels][3000]. */
+int mmz_log_mel_batch(const float* const* ys, const long* ns, int count, int n_mels, int threads, float* out,
+                      int* frames);
+/* A seeded synthetic 30 s clip: 1-8 sinusoids in 80-4000 Hz plus Gaussian noise at 10 dB SNR. */
+int mmz_synth_clip(unsigned long long seed, float* y, long n);
+
+/* ---------------------------------------------------------------- engine (src/model.rs, src/transcribe.rs) */
+
+typedef struct mmz_engine mmz_engine;
+
+/* src/model.rs:14-25 Dims */
+typedef struct {
+    int d, ff, heads, enc_layers, dec_layers, n_mels, vocab, max_t;
+} mmz_dims;
+
+/* src/model.rs:64-76 GenCfg (the prompt tokens are passed to mmz_engine_transcribe) */
+typedef struct {
+    int eos;
+    const int* suppress;     /* token ids never chosen */
+    int n_suppress;
+    int begin_suppress[2];   /* suppressed at the first generated position; -1 = none */
+    const int* align_heads;  /* n_align (decoder layer, head) pairs */
+    int n_align;
+} mmz_gencfg;
+
+/* Engine::new (src/model.rs:333-514) with seeded random-init weights in the reference's fused layouts, for up to
+ * bmax sequences and eg clips per encoder pass, on `device`. kernel_image NULL runs this library's sm_100a kernels;
+ * a path loads a fatbin exporting the reference's 23 kernel names (src/gpu.rs:16-40) and launches them by name with
+ * the reference's grid geometry. Returns NULL on error (mmz_last_error). */
+mmz_engine* mmz_engine_create(const mmz_dims* dims, const mmz_gencfg* gc, int bmax, int eg, int device,
+                              const char* kernel_image, unsigned long long seed);
+void mmz_engine_destroy(mmz_engine* e);
+/* transcribe (src/transcribe.rs:104-167) for n <= bmax clips: mel host [n][n_mels][3000] fp32, frames [n];
+ * prompt [np] tokens for every clip; at most max_steps decoding steps (<= max_t - 1; 0 = max_t - 1), stopping when
+ * every sequence has produced eos; use_graph replays one captured CUDA graph per step. Outputs: tokens [n][max_t],
+ * lens [n] (sequence lengths), times [n][max_t] (token start times, s); stage_s [3] = encode, decode, timestamps
+ * seconds (may be NULL). */
+int mmz_engine_transcribe(mmz_engine* e, const float* mel, const int* frames, int n, const int* prompt, int np,
+                          int max_steps, int use_graph, int threads, int* tokens, int* lens, float* times,
+                          double* stage_s);
+/* Engine::encode (src/model.rs:545-625) for gn <= eg clips of fp16 log-mel already on the device. */
+int mmz_engine_encode(mmz_engine* e, const void* mel16, int gn, int slot0);
+/* Engine::reset (src/model.rs:628-637): prompts [b][np]. */
+int mmz_engine_reset(mmz_engine* e, const int* prompts, int b, int np);
+/* Engine::step (src/model.rs:650-736), launched eagerly. */
+int mmz_engine_step(mmz_engine* e, int b, int prompt_len);
+/* Captures Engine::step as a CUDA graph (src/transcribe.rs:122-131); mmz_engine_replay launches it once. */
+int mmz_engine_capture(mmz_engine* e, int b, int prompt_len);
+int mmz_engine_replay(mmz_engine* e);
+/* Device address of an engine buffer: "tok", "done", "ctr", "align", "logits", "eh", "eqkv", "eatt", "xkv", "mel",
+ * "kc", "vc", "x", "hb", "att", "aslot"; NULL if unknown. */
+void* mmz_engine_buffer(mmz_engine* e, const char* name);
+void* mmz_engine_stream(mmz_engine* e);
+int mmz_engine_sync(mmz_engine* e);
+/* Device bytes the engine allocated. */
+long long mmz_engine_allocated(mmz_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

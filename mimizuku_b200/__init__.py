@@ -1,0 +1,239 @@
+"""mimizuku_b200: the B200-native attention hot path of the mimizuku Whisper engine.
+
+The product is the C-ABI library ``libmimizuku_b200.so`` (declared in ``include/mimizuku_b200.h``): sm_100a kernels
+for encoder flash attention (tcgen05/TMEM/TMA), decoder self- and cross-attention (cluster split-KV), fused
+residual-add + LayerNorm, the engine that drives them (a C++ restatement of the reference's model.rs and
+transcribe.rs) and the CPU timestamp stage (align.rs). This module binds it with ctypes under the reference's names
+(``enc_flash``, ``self_attn``, ``cross_attn``, ``layernorm``, ``add_layernorm``, ``jump_times``, ``dtw``, ``Engine``).
+
+Importing fails loudly when the library has not been built (``python -m mimizuku_b200.build``): there is no CPU or
+Python fallback for any of these functions.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmimizuku_b200.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is missing; build it with `python -m mimizuku_b200.build`")
+
+lib = ctypes.CDLL(LIB_PATH)
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_L = ctypes.c_long
+_LL = ctypes.c_longlong
+_F = ctypes.c_float
+_ULL = ctypes.c_ulonglong
+_IP = ctypes.POINTER(ctypes.c_int)
+_FP = ctypes.POINTER(ctypes.c_float)
+_DP = ctypes.POINTER(ctypes.c_double)
+
+
+class mmz_dims(ctypes.Structure):
+    _fields_ = [(n, _I) for n in ("d", "ff", "heads", "enc_layers", "dec_layers", "n_mels", "vocab", "max_t")]
+
+
+class mmz_gencfg(ctypes.Structure):
+    _fields_ = [("eos", _I), ("suppress", _IP), ("n_suppress", _I), ("begin_suppress", _I * 2),
+                ("align_heads", _IP), ("n_align", _I)]
+
+
+# name -> (restype, argtypes); every symbol include/mimizuku_b200.h declares
+SIGNATURES = {
+    "mmz_init": (_I, [_I]),
+    "mmz_last_error": (ctypes.c_char_p, []),
+    "mmz_status": (_I, [_IP]),
+    "mmz_set_wait_limit_ms": (_I, [_I, _I]),
+    "mmz_h2f": (_F, [ctypes.c_uint16]),
+    "mmz_f2h": (ctypes.c_uint16, [_F]),
+    "mmz_rh": (_F, [_F]),
+    "mmz_enc_flash": (_I, [_P, _P, _I, _I, _P]),
+    "mmz_self_attn": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
+    "mmz_kv_write": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
+    "mmz_cross_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "mmz_layernorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _P]),
+    "mmz_add_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _I, _F, _P]),
+    "mmz_jump_times": (_I, [_FP, _I, _I, _I, _I, _I, _FP]),
+    "mmz_dtw": (_I, [_DP, _I, _I, _IP, _IP, _IP]),
+    "mmz_log_mel": (_I, [_FP, _L, _I, _FP, _IP]),
+    "mmz_log_mel_batch": (_I, [ctypes.POINTER(_FP), ctypes.POINTER(_L), _I, _I, _I, _FP, _IP]),
+    "mmz_synth_clip": (_I, [_ULL, _FP, _L]),
+    "mmz_engine_create": (_P, [ctypes.POINTER(mmz_dims), ctypes.POINTER(mmz_gencfg), _I, _I, _I, ctypes.c_char_p,
+                               _ULL]),
+    "mmz_engine_destroy": (None, [_P]),
+    "mmz_engine_transcribe": (_I, [_P, _FP, _IP, _I, _IP, _I, _I, _I, _I, _IP, _IP, _FP, _DP]),
+    "mmz_engine_encode": (_I, [_P, _P, _I, _I]),
+    "mmz_engine_reset": (_I, [_P, _IP, _I, _I]),
+    "mmz_engine_step": (_I, [_P, _I, _I]),
+    "mmz_engine_capture": (_I, [_P, _I, _I]),
+    "mmz_engine_replay": (_I, [_P]),
+    "mmz_engine_buffer": (_P, [_P, ctypes.c_char_p]),
+    "mmz_engine_stream": (_P, [_P]),
+    "mmz_engine_sync": (_I, [_P]),
+    "mmz_engine_allocated": (_LL, [_P]),
+}
+
+for _name, (_res, _args) in SIGNATURES.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class MmzError(RuntimeError):
+    pass
+
+
+def _check(rc, what):
+    if rc != 0:
+        raise MmzError(f"{what}: {lib.mmz_last_error().decode()}")
+
+
+def _ptr(x):
+    """Device address of a torch tensor, an int address, or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def init(device=0):
+    _check(lib.mmz_init(device), "mmz_init")
+
+
+def status():
+    """Reads and clears the device status word: (code, kernel, site); code 0 = no error."""
+    out = (ctypes.c_int * 3)()
+    _check(lib.mmz_status(out), "mmz_status")
+    return tuple(out)
+
+
+def set_wait_limit_ms(device, ms):
+    _check(lib.mmz_set_wait_limit_ms(device, ms), "mmz_set_wait_limit_ms")
+
+
+# ------------------------------------------------------------------ fp16 helpers (src/gpu.rs:79-119)
+
+def h2f(h):
+    return lib.mmz_h2f(h)
+
+
+def f2h(x):
+    return lib.mmz_f2h(x)
+
+
+def rh(x):
+    return lib.mmz_rh(x)
+
+
+# ------------------------------------------------------------------ kernels (torch CUDA tensors or raw addresses)
+
+def enc_flash(qkv, out, d, groups=None, stream=None):
+    """kernels/whisper.cu:209 enc_flash: qkv [g][1500][3d] fp16 -> out [g][1500][d] fp16."""
+    g = groups if groups is not None else qkv.shape[0]
+    _check(lib.mmz_enc_flash(_ptr(qkv), _ptr(out), g, d, _stream(stream)), "enc_flash")
+
+
+def self_attn(qkv, kc, vc, out, ctr, done, max_t, d, batch=None, stream=None):
+    """kernels/whisper.cu:310-353 kv_write + self_attn (fused): position ctr[0]."""
+    b = batch if batch is not None else done.shape[0]
+    _check(lib.mmz_self_attn(_ptr(qkv), _ptr(kc), _ptr(vc), _ptr(out), _ptr(ctr), _ptr(done), b, max_t, d,
+                             _stream(stream)), "self_attn")
+
+
+def kv_write(qkv, kc, vc, ctr, max_t, d, batch, stream=None):
+    _check(lib.mmz_kv_write(_ptr(qkv), _ptr(kc), _ptr(vc), _ptr(ctr), batch, max_t, d, _stream(stream)), "kv_write")
+
+
+def cross_attn(q, kv, out, align, aslot, ctr, done, layer, nl, d, na, max_t, batch=None, stream=None):
+    """kernels/whisper.cu:368-449 cross_scores + cross_pv + cross_combine (fused)."""
+    b = batch if batch is not None else done.shape[0]
+    _check(lib.mmz_cross_attn(_ptr(q), _ptr(kv), _ptr(out), _ptr(align), _ptr(aslot), _ptr(ctr), _ptr(done), b, layer,
+                              nl, d, na, max_t, _stream(stream)), "cross_attn")
+
+
+def layernorm(x, w, b, out, eps=1e-5, rows=None, stream=None):
+    """kernels/whisper.cu:66 layernorm over the last dimension."""
+    dim = w.shape[-1]
+    r = rows if rows is not None else x.numel() // dim
+    _check(lib.mmz_layernorm(_ptr(x), _ptr(w), _ptr(b), _ptr(out), r, dim, eps, _stream(stream)), "layernorm")
+
+
+def add_layernorm(x, dx, w, b, out, eps=1e-5, rows=None, stream=None):
+    """kernels/whisper.cu:72 add_layernorm: x = h(x + dx), out = layernorm(x)."""
+    dim = w.shape[-1]
+    r = rows if rows is not None else x.numel() // dim
+    _check(lib.mmz_add_layernorm(_ptr(x), _ptr(dx), _ptr(w), _ptr(b), _ptr(out), r, dim, eps, _stream(stream)),
+           "add_layernorm")
+
+
+# ------------------------------------------------------------------ CPU stages
+
+def _fp(a):
+    return a.ctypes.data_as(_FP)
+
+
+def jump_times(w, cols, width=7):
+    """src/align.rs:8-63. w: float32 [rows][heads][cols_full] -> float32 [rows] start times (s)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, heads, cols_full = w.shape
+    out = np.zeros(rows, np.float32)
+    _check(lib.mmz_jump_times(_fp(w), rows, heads, cols_full, cols, width, _fp(out)), "jump_times")
+    return out
+
+
+def dtw(m):
+    """src/align.rs:66-106 on a float64 cost matrix [rows][cols] -> (text, time) int arrays."""
+    m = np.ascontiguousarray(m, dtype=np.float64)
+    rows, cols = m.shape
+    text = np.zeros(rows + cols + 1, np.int32)
+    time = np.zeros(rows + cols + 1, np.int32)
+    n = ctypes.c_int(0)
+    _check(lib.mmz_dtw(m.ctypes.data_as(_DP), rows, cols, text.ctypes.data_as(_IP), time.ctypes.data_as(_IP),
+                       ctypes.byref(n)), "dtw")
+    return text[:n.value].copy(), time[:n.value].copy()
+
+
+def log_mel(y, n_mels):
+    """src/audio.rs:192-237: float32 samples at 16 kHz -> (log-mel [n_mels][3000], frames)."""
+    y = np.ascontiguousarray(y, dtype=np.float32)
+    out = np.zeros((n_mels, 3000), np.float32)
+    fr = ctypes.c_int(0)
+    _check(lib.mmz_log_mel(_fp(y), len(y), n_mels, _fp(out), ctypes.byref(fr)), "log_mel")
+    return out, fr.value
+
+
+def log_mel_batch(clips, n_mels, threads=0):
+    clips = [np.ascontiguousarray(c, dtype=np.float32) for c in clips]
+    n = len(clips)
+    out = np.zeros((n, n_mels, 3000), np.float32)
+    frames = np.zeros(n, np.int32)
+    ptrs = (_FP * n)(*[_fp(c) for c in clips])
+    lens = (_L * n)(*[len(c) for c in clips])
+    _check(lib.mmz_log_mel_batch(ptrs, lens, n, n_mels, threads, _fp(out), frames.ctypes.data_as(_IP)),
+           "log_mel_batch")
+    return out, frames
+
+
+def synth_clip(seed, n=480000):
+    y = np.zeros(n, np.float32)
+    _check(lib.mmz_synth_clip(seed, _fp(y), n), "synth_clip")
+    return y
+
+
+# ------------------------------------------------------------------ engine
+
+from .engine import Engine, ModelConfig, LARGE_V3, LARGE_V3_TURBO, TINY  # noqa: E402,F401

@@ -1,0 +1,760 @@
+// The Whisper engine (see engine.h): weights, buffers and the encoder / decoder-step launch sequences of the
+// reference's src/model.rs, the batch driver of src/transcribe.rs, and the two kernel images it can run on.
+#include "engine.h"
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <iterator>
+#include <thread>
+
+#include "host_cpu.h"
+#include "launch.h"
+
+namespace mmz {
+
+constexpr int HDIM = 64;
+constexpr int TENC_ = 1500;
+constexpr int NFRAMES = 3000;
+constexpr int NCH = (TENC_ + 63) / 64;
+constexpr float EPS = 1e-5f;            // model.rs:12
+constexpr size_t WS_BYTES = 64u << 20;  // fixed cuBLAS workspace: no allocation during graph capture (gpu.rs:41)
+
+// ============================================================================ kernel images
+
+class Kernels {
+   public:
+    virtual ~Kernels() {}
+    virtual bool native() const = 0;
+    virtual int layernorm(const void* x, const Ln& l, void* y, int rows, int d, cudaStream_t st) = 0;
+    virtual int add_layernorm(void* x, const void* dx, const Ln& l, void* y, int rows, int d, cudaStream_t st) = 0;
+    virtual int enc_attn(const void* qkv, void* out, int gn, int d, int nh, cudaStream_t st) = 0;
+    virtual int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b,
+                          int maxT, int d, int nh, cudaStream_t st) = 0;
+    virtual int cross_attn(const void* xq, const void* kv, void* s, void* stat, void* part, void* att, void* align,
+                           const int* aslot, const int* ctr, const int* done, int b, int layer, int nl, int d, int nh,
+                           int na, int maxT, cudaStream_t st) = 0;
+    virtual int embed(const int* tok, const int* ctr, const void* emb, const void* dpos, void* x, int b, int maxT,
+                      int d, cudaStream_t st) = 0;
+    virtual int argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
+                           int b, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) = 0;
+    virtual int advance(int* ctr, cudaStream_t st) = 0;
+    virtual int im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) = 0;
+    virtual int im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) = 0;
+    virtual int gelu(void* x, long n, cudaStream_t st) = 0;
+    virtual int add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) = 0;
+    virtual int fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st) = 0;
+    virtual int fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) = 0;
+    // y = x W^T + bias for m <= 8 rows, or -2 when the image has no such kernel
+    virtual int gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+                     cudaStream_t st) = 0;
+};
+
+// ---------------------------------------------------------------- native sm_100a kernels
+
+class NativeKernels : public Kernels {
+   public:
+    bool native() const override { return true; }
+    int layernorm(const void* x, const Ln& l, void* y, int rows, int d, cudaStream_t st) override {
+        return launch_layernorm(x, l.w, l.b, y, rows, d, EPS, st);
+    }
+    int add_layernorm(void* x, const void* dx, const Ln& l, void* y, int rows, int d, cudaStream_t st) override {
+        return launch_add_layernorm(x, dx, l.w, l.b, y, rows, d, EPS, st);
+    }
+    int enc_attn(const void* qkv, void* out, int gn, int d, int, cudaStream_t st) override {
+        return launch_enc_flash(qkv, out, gn, d, st);
+    }
+    // kv_write is folded into the self-attention kernel
+    int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b, int maxT,
+                  int d, int, cudaStream_t st) override {
+        return launch_self_attn(qkv, kc, vc, att, ctr, done, b, maxT, d, st);
+    }
+    // one fused kernel; the reference's S / stat / part scratch is not needed
+    int cross_attn(const void* xq, const void* kv, void*, void*, void*, void* att, void* align, const int* aslot,
+                   const int* ctr, const int* done, int b, int layer, int nl, int d, int, int na, int maxT,
+                   cudaStream_t st) override {
+        return launch_cross_attn(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, st);
+    }
+    int embed(const int* tok, const int* ctr, const void* emb, const void* dpos, void* x, int b, int maxT, int d,
+              cudaStream_t st) override {
+        return launch_embed(tok, ctr, emb, dpos, x, b, maxT, d, st);
+    }
+    int argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr, int b,
+                   int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) override {
+        return launch_argmax_tok(logits, V, sup, tok, done, ctr, b, maxT, prompt_len, eos, bs1, bs2, st);
+    }
+    int advance(int* ctr, cudaStream_t st) override { return launch_advance(ctr, st); }
+    int im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) override {
+        return launch_im2col1(mel, X, n, nm, st);
+    }
+    int im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) override {
+        return launch_im2col2(h1, X, n, d, st);
+    }
+    int gelu(void* x, long n, cudaStream_t st) override { return launch_gelu(x, n, st); }
+    int add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) override {
+        return launch_add_pos(x, pos, rows, n, period, st);
+    }
+    int fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st) override {
+        return launch_fill_bias(y, bias, rows, n, ld, st);
+    }
+    int fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) override {
+        return launch_fill_bias_heads(y, bias, n8, st);
+    }
+    int gemv(const void*, int, const void*, void*, int, int, int, int, const void*, cudaStream_t) override { return -2; }
+};
+
+// ---------------------------------------------------------------- a fatbin with the reference's kernel names
+
+typedef CUresult (*PfnModuleLoadData)(CUmodule*, const void*);
+typedef CUresult (*PfnModuleUnload)(CUmodule);
+typedef CUresult (*PfnModuleGetFunction)(CUfunction*, CUmodule, const char*);
+typedef CUresult (*PfnLaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned,
+                                    CUstream, void**, void**);
+
+static void* driver_fn(const char* name) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+        return nullptr;
+    return p;
+}
+
+// One launch argument as the reference's host passes it (gpu.rs:44-50): u64 pointer, i32, i64 or f32.
+struct Arg {
+    union {
+        uint64_t p;
+        int32_t i;
+        int64_t l;
+        float f;
+    } v;
+    static Arg P(const void* x) { Arg a; a.v.p = (uint64_t)(uintptr_t)x; return a; }
+    static Arg I(int x) { Arg a; a.v.l = 0; a.v.i = x; return a; }
+    static Arg L(long long x) { Arg a; a.v.l = x; return a; }
+    static Arg F(float x) { Arg a; a.v.l = 0; a.v.f = x; return a; }
+};
+
+class FatbinKernels : public Kernels {
+   public:
+    std::string err;
+    explicit FatbinKernels(const char* path) {
+        load_ = (PfnModuleLoadData)driver_fn("cuModuleLoadData");
+        unload_ = (PfnModuleUnload)driver_fn("cuModuleUnload");
+        getfn_ = (PfnModuleGetFunction)driver_fn("cuModuleGetFunction");
+        launch_ = (PfnLaunchKernel)driver_fn("cuLaunchKernel");
+        if (!load_ || !getfn_ || !launch_ || !unload_) {
+            err = "driver entry points unavailable";
+            return;
+        }
+        std::ifstream f(path, std::ios::binary);
+        if (!f) {
+            err = std::string("cannot read kernel image ") + path;
+            return;
+        }
+        image_.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+        if (load_(&mod_, image_.data()) != CUDA_SUCCESS) {
+            err = std::string("cuModuleLoadData failed for ") + path;
+            return;
+        }
+        // gpu.rs:16-40: a missing name is an error at start-up
+        static const char* names[] = {"layernorm", "add_layernorm", "add_inplace", "fill_bias", "fill_bias_heads",
+                                      "gelu_inplace", "add_pos", "im2col1", "im2col2", "softmax_rows", "enc_flash",
+                                      "embed", "kv_write", "self_attn", "cross_scores", "cross_pv", "cross_combine",
+                                      "argmax_tok", "advance", "gemv_1", "gemv_2", "gemv_4", "gemv_8"};
+        for (const char* n : names) {
+            CUfunction fn;
+            if (getfn_(&fn, mod_, n) != CUDA_SUCCESS) {
+                err = std::string("kernel image has no function ") + n;
+                return;
+            }
+            fns_.push_back({n, fn});
+        }
+    }
+    ~FatbinKernels() override {
+        if (mod_ && unload_) unload_(mod_);
+    }
+    bool native() const override { return false; }
+
+    // gpu.rs:187-201
+    int k(const char* name, unsigned gx, unsigned gy, unsigned gz, unsigned block, unsigned smem, cudaStream_t st,
+          std::initializer_list<Arg> args) {
+        CUfunction fn = nullptr;
+        for (auto& e : fns_)
+            if (!strcmp(e.first, name)) fn = e.second;
+        if (!fn) return failf("no kernel %s", name);
+        std::vector<Arg> vals(args);
+        std::vector<void*> ptrs;
+        for (auto& a : vals) ptrs.push_back(&a.v);
+        CUresult r = launch_(fn, gx, gy, gz, block, 1, 1, smem, (CUstream)st, ptrs.data(), nullptr);
+        return r == CUDA_SUCCESS ? 0 : failf("%s: cuLaunchKernel failed (%d)", name, (int)r);
+    }
+    // elementwise launch over n items (gpu.rs:203-206)
+    int k1(const char* name, long n, cudaStream_t st, std::initializer_list<Arg> args) {
+        return k(name, (unsigned)((n + 255) / 256), 1, 1, 256, 0, st, args);
+    }
+
+    int layernorm(const void* x, const Ln& l, void* y, int rows, int d, cudaStream_t st) override {
+        return k("layernorm", rows, 1, 1, 128, 0, st, {Arg::P(x), Arg::P(l.w), Arg::P(l.b), Arg::P(y), Arg::I(d), Arg::F(EPS)});
+    }
+    int add_layernorm(void* x, const void* dx, const Ln& l, void* y, int rows, int d, cudaStream_t st) override {
+        return k("add_layernorm", rows, 1, 1, 128, 0, st,
+                 {Arg::P(x), Arg::P(dx), Arg::P(l.w), Arg::P(l.b), Arg::P(y), Arg::I(d), Arg::F(EPS)});
+    }
+    // model.rs:566
+    int enc_attn(const void* qkv, void* out, int gn, int d, int nh, cudaStream_t st) override {
+        return k("enc_flash", (TENC_ + 63) / 64, nh, gn, 128, 0, st, {Arg::P(qkv), Arg::P(out), Arg::I(d)});
+    }
+    // model.rs:665-672
+    int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b, int maxT,
+                  int d, int nh, cudaStream_t st) override {
+        if (k("kv_write", b, 1, 1, 256, 0, st, {Arg::P(qkv), Arg::P(kc), Arg::P(vc), Arg::P(ctr), Arg::I(maxT), Arg::I(d)}))
+            return -1;
+        return k("self_attn", b, nh, 1, 128, 0, st,
+                 {Arg::P(qkv), Arg::P(kc), Arg::P(vc), Arg::P(att), Arg::P(ctr), Arg::P(done), Arg::I(maxT), Arg::I(d)});
+    }
+    // model.rs:676-705
+    int cross_attn(const void* xq, const void* kv, void* s, void* stat, void* part, void* att, void* align,
+                   const int* aslot, const int* ctr, const int* done, int b, int layer, int nl, int d, int nh, int na,
+                   int maxT, cudaStream_t st) override {
+        if (k("cross_scores", b * nh, NCH, 1, 128, 0, st,
+              {Arg::P(xq), Arg::P(kv), Arg::P(s), Arg::P(stat), Arg::P(done), Arg::I(layer), Arg::I(nl), Arg::I(d)}))
+            return -1;
+        if (k("cross_pv", b * nh, NCH, 1, 128, 0, st,
+              {Arg::P(s), Arg::P(stat), Arg::P(kv), Arg::P(part), Arg::P(align), Arg::P(aslot), Arg::P(ctr),
+               Arg::P(done), Arg::I(layer), Arg::I(nl), Arg::I(d), Arg::I(na), Arg::I(maxT)}))
+            return -1;
+        return k("cross_combine", b * nh, 1, 1, HDIM, 0, st, {Arg::P(part), Arg::P(att), Arg::P(done), Arg::I(d)});
+    }
+    int embed(const int* tok, const int* ctr, const void* emb, const void* dpos, void* x, int b, int maxT, int d,
+              cudaStream_t st) override {
+        return k("embed", b, 1, 1, 256, 0, st,
+                 {Arg::P(tok), Arg::P(ctr), Arg::P(emb), Arg::P(dpos), Arg::P(x), Arg::I(maxT), Arg::I(d)});
+    }
+    int argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr, int b,
+                   int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) override {
+        return k("argmax_tok", b, 1, 1, 1024, 0, st,
+                 {Arg::P(logits), Arg::I(V), Arg::P(sup), Arg::P(tok), Arg::P(done), Arg::P(ctr), Arg::I(maxT),
+                  Arg::I(prompt_len), Arg::I(eos), Arg::I(bs1), Arg::I(bs2)});
+    }
+    int advance(int* ctr, cudaStream_t st) override { return k("advance", 1, 1, 1, 1, 0, st, {Arg::P(ctr)}); }
+    int im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) override {
+        return k1("im2col1", n, st, {Arg::P(mel), Arg::P(X), Arg::L(n), Arg::I(nm)});
+    }
+    int im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) override {
+        return k1("im2col2", n, st, {Arg::P(h1), Arg::P(X), Arg::L(n), Arg::I(d)});
+    }
+    int gelu(void* x, long n, cudaStream_t st) override {
+        return k1("gelu_inplace", n / 2, st, {Arg::P(x), Arg::L(n / 2)});
+    }
+    int add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) override {
+        return k1("add_pos", rows * n, st, {Arg::P(x), Arg::P(pos), Arg::L(rows), Arg::I(n), Arg::I(period)});
+    }
+    int fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st) override {
+        return k1("fill_bias", rows * n / 8, st, {Arg::P(y), Arg::P(bias), Arg::L(rows), Arg::I(n), Arg::L(ld)});
+    }
+    int fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) override {
+        return k1("fill_bias_heads", n8, st, {Arg::P(y), Arg::P(bias), Arg::L(n8)});
+    }
+    // gpu.rs:211-228
+    int gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int kk, const void* bias,
+             cudaStream_t st) override {
+        const char* name;
+        int mr, kc;
+        if (m == 1) { name = "gemv_1"; mr = 1; kc = 2048; }
+        else if (m == 2) { name = "gemv_2"; mr = 2; kc = 2048; }
+        else if (m <= 4) { name = "gemv_4"; mr = 4; kc = 1024; }
+        else { name = "gemv_8"; mr = 8; kc = 1024; }
+        const int per_block = 8 * 4;
+        return k(name, (n + per_block - 1) / per_block, 1, 1, 256, mr * kc * 2, st,
+                 {Arg::P(x), Arg::I(ldx), Arg::P(w), Arg::P(y), Arg::I(ldy), Arg::I(m), Arg::I(n), Arg::I(kk), Arg::P(bias)});
+    }
+
+   private:
+    PfnModuleLoadData load_ = nullptr;
+    PfnModuleUnload unload_ = nullptr;
+    PfnModuleGetFunction getfn_ = nullptr;
+    PfnLaunchKernel launch_ = nullptr;
+    CUmodule mod_ = nullptr;
+    std::vector<char> image_;
+    std::vector<std::pair<const char*, CUfunction>> fns_;
+};
+
+// ============================================================================ engine
+
+#define CK(x)                                        \
+    do {                                             \
+        if ((x) != 0) return -1;                     \
+    } while (0)
+#define CUDA_CK(x)                                                                                  \
+    do {                                                                                            \
+        cudaError_t e_ = (x);                                                                       \
+        if (e_ != cudaSuccess) return failf("%s:%d: %s", __FILE__, __LINE__, cudaGetErrorString(e_)); \
+    } while (0)
+
+void* Engine::alloc(size_t bytes) {
+    void* p = nullptr;
+    bytes = bytes < 16 ? 16 : bytes;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    cudaMemsetAsync(p, 0, bytes, st_);
+    allocs_.push_back(p);
+    allocated_ += bytes;
+    return p;
+}
+
+Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char* kernel_image, unsigned long long seed)
+    : dm_(dims), gc_(gc), bmax_(bmax), eg_(eg) {
+    const int d = dm_.d, ff = dm_.ff, nh = dm_.nh, nl = dm_.dec_layers, mt = dm_.max_t;
+    // model.rs:47-59
+    if (nh * HDIM != d || d % 128 || ff % 8 || mt < 16 || mt > 448 || dm_.enc_layers < 1 || dm_.enc_layers > 64 ||
+        nl < 1 || nl > 64 || bmax < 1 || eg < 1 || eg > bmax || dm_.vocab < 1 || dm_.n_mels < 1) {
+        err_ = "unsupported shape";
+        return;
+    }
+    for (auto& ah : gc_.align_heads)
+        if (ah.first < 0 || ah.first >= nl || ah.second < 0 || ah.second >= nh) {
+            err_ = "alignment head out of range";
+            return;
+        }
+    if (gc_.align_heads.empty()) {
+        err_ = "no alignment heads";
+        return;
+    }
+    if (cudaGetDevice(&dev_) != cudaSuccess) {
+        err_ = "no CUDA device";
+        return;
+    }
+    if (kernel_image && *kernel_image) {
+        auto fk = new FatbinKernels(kernel_image);
+        k_.reset(fk);
+        if (!fk->err.empty()) {
+            err_ = fk->err;
+            return;
+        }
+    } else {
+        DevCtx& dc = dev_ctx();
+        if (!dc.ok) {
+            err_ = dc.err;
+            return;
+        }
+        k_.reset(new NativeKernels());
+    }
+    if (cudaStreamCreateWithFlags(&st_, cudaStreamNonBlocking) != cudaSuccess || cublasCreate(&blas_) != CUBLAS_STATUS_SUCCESS ||
+        cublasSetStream(blas_, st_) != CUBLAS_STATUS_SUCCESS) {
+        err_ = "stream / cuBLAS setup failed";
+        return;
+    }
+    ws_ = alloc(WS_BYTES);
+    if (!ws_ || cublasSetWorkspace(blas_, ws_, WS_BYTES) != CUBLAS_STATUS_SUCCESS) {
+        err_ = "cuBLAS workspace";
+        return;
+    }
+    const int na = (int)gc_.align_heads.size();
+    auto H = [&](size_t n) { return alloc(n * 2); };
+    const size_t r1 = (size_t)eg * NFRAMES, r2 = (size_t)eg * TENC_;
+    mel_ = H((size_t)eg * dm_.n_mels * NFRAMES);
+    mel32_ = (float*)alloc((size_t)eg * dm_.n_mels * NFRAMES * 4);
+    x1_ = H(r1 * 3 * dm_.n_mels);
+    h1_ = H(r1 * d);
+    x2_ = H(r2 * 3 * d);
+    ex_ = H(r2 * d);
+    eh_ = H(r2 * d);
+    eqkv_ = H(r2 * 3 * d);
+    eatt_ = H(r2 * d);
+    ef_ = H(r2 * ff);
+    const size_t b = bmax;
+    xkv_buf_ = H(b * nl * 2 * d * TENC_);
+    tok_ = (int*)alloc(b * mt * 4);
+    done_ = (int*)alloc(b * 4);
+    ctr_ = (int*)alloc(16);
+    x_ = H(b * d);
+    hb_ = H(b * d);
+    att_ = H(b * d);
+    dout_ = H((size_t)nl * b * (7 * d + ff));
+    dbias_ = H((size_t)nl * b * (7 * d + ff));
+    logits_ = H(b * dm_.vocab);
+    kc_ = H((size_t)nl * b * mt * d);
+    vc_ = H((size_t)nl * b * mt * d);
+    if (!k_->native()) {  // the reference's split cross-attention scratch (model.rs:452-454)
+        s_ = alloc(b * nh * TENC_ * 4);
+        stat_ = alloc(b * nh * NCH * 8);
+        part_ = alloc(b * nh * NCH * HDIM * 4);
+    } else {
+        s_ = stat_ = part_ = nullptr;
+    }
+    align_ = H(b * mt * na * TENC_);
+    for (void* p : {mel_, (void*)mel32_, x1_, h1_, x2_, ex_, eh_, eqkv_, eatt_, ef_, xkv_buf_, (void*)tok_, (void*)done_, (void*)ctr_,
+                    x_, hb_, att_, dout_, dbias_, logits_, kc_, vc_, align_})
+        if (!p) {
+            err_ = "device memory allocation failed";
+            return;
+        }
+    // suppress mask and alignment slots (model.rs:411-425)
+    std::vector<unsigned char> sup(dm_.vocab, 0);
+    for (int t : gc_.suppress)
+        if (t >= 0 && t < dm_.vocab) sup[t] = 1;
+    sup_ = (unsigned char*)alloc(dm_.vocab);
+    std::vector<int> slots(nl * nh, -1);
+    for (int s = 0; s < na; s++) slots[gc_.align_heads[s].first * nh + gc_.align_heads[s].second] = s;
+    aslot_ = (int*)alloc(slots.size() * 4);
+    if (!sup_ || !aslot_) {
+        err_ = "device memory allocation failed";
+        return;
+    }
+    cudaMemcpyAsync(sup_, sup.data(), sup.size(), cudaMemcpyHostToDevice, st_);
+    cudaMemcpyAsync(aslot_, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice, st_);
+    cudaStreamSynchronize(st_);
+    if (init_weights(seed)) {
+        err_ = std::string("weight initialisation failed: ") + last_error();
+        return;
+    }
+    // bias images of every decoder layer's outputs (model.rs:505-511)
+    for (int i = 0; i < nl; i++) {
+        const DecLayer& l = dec_[i];
+        const std::pair<int, const Lin*> outs[6] = {{3 * d, &l.qkv}, {d, &l.o}, {d, &l.xq}, {d, &l.xo}, {ff, &l.fc1}, {d, &l.fc2}};
+        for (int o = 0; o < 6; o++) {
+            void* dst = (char*)dbias_ + ((char*)dec_out(i, o) - (char*)dout_);
+            if (k_->fill_bias(dst, outs[o].second->b, bmax, outs[o].first, outs[o].first, st_)) {
+                err_ = last_error();
+                return;
+            }
+        }
+    }
+    if (cudaStreamSynchronize(st_) != cudaSuccess) err_ = "engine set-up failed";
+}
+
+Engine::~Engine() {
+    if (graph_) cudaGraphExecDestroy(graph_);
+    if (st_) cudaStreamSynchronize(st_);
+    k_.reset();
+    for (void* p : allocs_) cudaFree(p);
+    if (blas_) cublasDestroy(blas_);
+    if (st_) cudaStreamDestroy(st_);
+}
+
+// Random-init weights with the fused layouts of model.rs:253-264 (qkv [3d][d], bias [q, 0, v]) and :387-399 (every
+// decoder layer's cross k/v projection fused: [nl * 2d][d], bias [0, v] per layer). Linear weights and embeddings
+// N(0, 0.02), biases N(0, 0.02), layer-norm weights N(1, 0.02) and biases N(0, 0.02); the encoder positions are
+// Whisper's sinusoids. One allocation per tensor class, seeded per tensor.
+int Engine::init_weights(unsigned long long seed) {
+    const int d = dm_.d, ff = dm_.ff, nm = dm_.n_mels, nl = dm_.dec_layers;
+    unsigned long long tid = 0;
+    auto normal = [&](size_t n, float mean, float std) -> void* {
+        void* p = alloc(n * 2);
+        if (!p) return nullptr;
+        if (launch_fill_normal(p, (long)n, seed * 1000003ull + (++tid), mean, std, st_)) return nullptr;
+        return p;
+    };
+    auto ln = [&](Ln& l) { l.w = normal(d, 1.f, 0.02f); l.b = normal(d, 0.f, 0.02f); return l.w && l.b; };
+    auto lin = [&](Lin& l, size_t n, size_t k) { l.w = normal(n * k, 0.f, 0.02f); l.b = normal(n, 0.f, 0.02f); return l.w && l.b; };
+    auto qkv = [&](Lin& l) {
+        if (!lin(l, 3 * (size_t)d, d)) return false;
+        return cudaMemsetAsync((char*)l.b + (size_t)d * 2, 0, (size_t)d * 2, st_) == cudaSuccess;  // k_proj has no bias
+    };
+    enc_.resize(dm_.enc_layers);
+    for (auto& l : enc_)
+        if (!ln(l.ln1) || !qkv(l.qkv) || !lin(l.o, d, d) || !ln(l.ln2) || !lin(l.fc1, ff, d) || !lin(l.fc2, d, ff)) return -1;
+    dec_.resize(nl);
+    for (auto& l : dec_)
+        if (!ln(l.ln1) || !qkv(l.qkv) || !lin(l.o, d, d) || !ln(l.lnx) || !lin(l.xq, d, d) || !lin(l.xo, d, d) ||
+            !ln(l.ln3) || !lin(l.fc1, ff, d) || !lin(l.fc2, d, ff))
+            return -1;
+    if (!lin(xkv_, (size_t)nl * 2 * d, d)) return -1;
+    for (int i = 0; i < nl; i++) cudaMemsetAsync((char*)xkv_.b + (size_t)i * 2 * d * 2, 0, (size_t)d * 2, st_);
+    if (!lin(conv1_, d, (size_t)nm * 3) || !lin(conv2_, d, (size_t)d * 3) || !ln(eln_) || !ln(dln_)) return -1;
+    emb_ = normal((size_t)dm_.vocab * d, 0.f, 0.02f);
+    dpos_ = normal((size_t)dm_.max_t * d, 0.f, 0.02f);
+    if (!emb_ || !dpos_) return -1;
+    // sinusoids(1500, d): [sin(t * inc_i) | cos(t * inc_i)], inc_i = exp(-log(10000) / (d/2 - 1) * i)
+    std::vector<uint16_t> pos((size_t)TENC_ * d);
+    const int half = d / 2;
+    for (int t = 0; t < TENC_; t++)
+        for (int i = 0; i < half; i++) {
+            const double inv = std::exp(-std::log(10000.0) / (half - 1) * i);
+            pos[(size_t)t * d + i] = f2h((float)std::sin(t * inv));
+            pos[(size_t)t * d + half + i] = f2h((float)std::cos(t * inv));
+        }
+    epos_ = alloc(pos.size() * 2);
+    if (!epos_) return -1;
+    CUDA_CK(cudaMemcpyAsync(epos_, pos.data(), pos.size() * 2, cudaMemcpyHostToDevice, st_));
+    CUDA_CK(cudaStreamSynchronize(st_));
+    return 0;
+}
+
+// decoder layer i's output `which` (qkv, o, xq, xo, fc1, fc2) inside dout, [bmax][n] each (model.rs:516-522)
+void* Engine::dec_out(int i, int which) const {
+    const size_t d = dm_.d, ff = dm_.ff, b = bmax_;
+    const size_t offs[6] = {0, 3 * d, 4 * d, 5 * d, 6 * d, 6 * d + ff};
+    return (char*)dout_ + 2 * (i * b * (7 * d + ff)) + 2 * b * offs[which];
+}
+
+// column-major strided-batched fp16 GEMM, fp32 accumulation (gpu.rs:254-286)
+int Engine::matmul(bool ta, bool tb, int m, int n, int k, float alpha, const void* a, int lda, long long sa,
+                   const void* b, int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch) {
+    cublasStatus_t r = cublasGemmStridedBatchedEx(
+        blas_, ta ? CUBLAS_OP_T : CUBLAS_OP_N, tb ? CUBLAS_OP_T : CUBLAS_OP_N, m, n, k, &alpha, a, CUDA_R_16F, lda, sa,
+        b, CUDA_R_16F, ldb, sb, &beta, c, CUDA_R_16F, ldc, sc, batch, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    return r == CUBLAS_STATUS_SUCCESS ? 0 : failf("cublasGemmStridedBatchedEx failed (%d)", (int)r);
+}
+
+// y = x W^T + bias: bias first, then the GEMM accumulates onto it (beta = 1), one rounding of acc + bias
+// (gpu.rs:208-236); m <= 8 goes to the image's gemv kernels where it has them
+int Engine::lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k) {
+    if (m <= 8) {
+        int r = k_->gemv(x, ldx, l.w, y, ldy, m, n, k, l.b, st_);
+        if (r != -2) return r;
+    }
+    CK(k_->fill_bias(y, l.b, m, n, ldy, st_));
+    return matmul(true, false, n, m, k, 1.f, l.w, k, 0, x, ldx, 0, 1.f, y, ldy, 0, 1);
+}
+
+// the same for a y that already holds the bias (gpu.rs:238-247)
+int Engine::lin_onto_bias(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k) {
+    if (m <= 8) {
+        int r = k_->gemv(x, ldx, l.w, y, ldy, m, n, k, l.b, st_);
+        if (r != -2) return r;
+    }
+    return matmul(true, false, n, m, k, 1.f, l.w, k, 0, x, ldx, 0, 1.f, y, ldy, 0, 1);
+}
+
+// model.rs:543-625
+int Engine::encode_dev(const void* mel16, int gn, int slot0) {
+    if (gn < 1 || gn > eg_ || slot0 < 0 || slot0 + gn > bmax_) return fail("encode: bad group");
+    const int d = dm_.d, nm = dm_.n_mels, nh = dm_.nh, ff = dm_.ff, nl = dm_.dec_layers;
+    const long r1 = (long)gn * NFRAMES, r2 = (long)gn * TENC_;
+    if (mel16 != mel_) CUDA_CK(cudaMemcpyAsync(mel_, mel16, (size_t)gn * nm * NFRAMES * 2, cudaMemcpyDeviceToDevice, st_));
+    CK(k_->im2col1(mel_, x1_, r1 * 3 * nm, nm, st_));
+    CK(lin(x1_, 3 * nm, conv1_, h1_, d, r1, d, 3 * nm));
+    CK(k_->gelu(h1_, r1 * d, st_));
+    CK(k_->im2col2(h1_, x2_, r2 * 3 * d, d, st_));
+    CK(lin(x2_, 3 * d, conv2_, ex_, d, r2, d, 3 * d));
+    CK(k_->gelu(ex_, r2 * d, st_));
+    CK(k_->add_pos(ex_, epos_, r2, d, TENC_, st_));
+    CK(k_->layernorm(ex_, enc_[0].ln1, eh_, r2, d, st_));
+    for (size_t i = 0; i < enc_.size(); i++) {
+        const EncLayer& l = enc_[i];
+        CK(lin(eh_, d, l.qkv, eqkv_, 3 * d, r2, 3 * d, d));
+        CK(k_->enc_attn(eqkv_, eatt_, gn, d, nh, st_));
+        CK(lin(eatt_, d, l.o, eh_, d, r2, d, d));
+        CK(k_->add_layernorm(ex_, eh_, l.ln2, eh_, r2, d, st_));
+        CK(lin(eh_, d, l.fc1, ef_, ff, r2, ff, d));
+        CK(k_->gelu(ef_, r2 * ff, st_));
+        CK(lin(ef_, ff, l.fc2, eh_, d, r2, d, ff));
+        const Ln& next = i + 1 < enc_.size() ? enc_[i + 1].ln1 : eln_;
+        CK(k_->add_layernorm(ex_, eh_, next, eh_, r2, d, st_));
+    }
+    // cross k/v per (layer, k|v, head) as [position][64] blocks: one batched GEMM per clip onto the bias (:614-623)
+    const long xkv = (long)nl * 2 * d * TENC_;
+    const int nblk = nl * 2 * nh;
+    for (int c = 0; c < gn; c++) {
+        void* dst = (char*)xkv_buf_ + 2 * (size_t)(slot0 + c) * xkv;
+        CK(k_->fill_bias_heads(dst, xkv_.b, xkv / 8, st_));
+        CK(matmul(true, false, HDIM, TENC_, d, 1.f, xkv_.w, d, (long long)HDIM * d, (char*)eh_ + 2 * (size_t)c * TENC_ * d,
+                  d, 0, 1.f, dst, HDIM, (long long)TENC_ * HDIM, nblk));
+    }
+    return 0;
+}
+
+int Engine::reset(const int* prompts, int b, int np) {
+    if (b < 1 || b > bmax_ || np < 1 || np >= dm_.max_t) return fail("reset: bad batch or prompt");
+    const int mt = dm_.max_t;
+    std::vector<int> t((size_t)b * mt, 0);
+    for (int s = 0; s < b; s++) std::memcpy(&t[(size_t)s * mt], prompts + (size_t)s * np, np * 4);
+    CUDA_CK(cudaMemcpyAsync(tok_, t.data(), t.size() * 4, cudaMemcpyHostToDevice, st_));
+    CUDA_CK(cudaMemsetAsync(done_, 0, (size_t)b * 4, st_));
+    CUDA_CK(cudaMemsetAsync(ctr_, 0, 16, st_));
+    CUDA_CK(cudaStreamSynchronize(st_));
+    return 0;
+}
+
+// model.rs:648-736
+int Engine::step(int b, int prompt_len) {
+    const int d = dm_.d, ff = dm_.ff, nh = dm_.nh, nl = dm_.dec_layers, mt = dm_.max_t;
+    const int na = (int)gc_.align_heads.size();
+    CK(k_->embed(tok_, ctr_, emb_, dpos_, x_, b, mt, d, st_));
+    CK(k_->layernorm(x_, dec_[0].ln1, hb_, b, d, st_));
+    CUDA_CK(cudaMemcpyAsync(dout_, dbias_, (size_t)2 * nl * bmax_ * (7 * d + ff), cudaMemcpyDeviceToDevice, st_));
+    for (int i = 0; i < nl; i++) {
+        const DecLayer& l = dec_[i];
+        void* kc = (char*)kc_ + 2 * (size_t)i * bmax_ * mt * d;
+        void* vc = (char*)vc_ + 2 * (size_t)i * bmax_ * mt * d;
+        void *oqkv = dec_out(i, 0), *oo = dec_out(i, 1), *oxq = dec_out(i, 2), *oxo = dec_out(i, 3),
+             *ofc1 = dec_out(i, 4), *ofc2 = dec_out(i, 5);
+        CK(lin_onto_bias(hb_, d, l.qkv, oqkv, 3 * d, b, 3 * d, d));
+        CK(k_->self_attn(oqkv, kc, vc, att_, ctr_, done_, b, mt, d, nh, st_));
+        CK(lin_onto_bias(att_, d, l.o, oo, d, b, d, d));
+        CK(k_->add_layernorm(x_, oo, l.lnx, hb_, b, d, st_));
+        CK(lin_onto_bias(hb_, d, l.xq, oxq, d, b, d, d));
+        CK(k_->cross_attn(oxq, xkv_buf_, s_, stat_, part_, att_, align_, aslot_, ctr_, done_, b, i, nl, d, nh, na, mt, st_));
+        CK(lin_onto_bias(att_, d, l.xo, oxo, d, b, d, d));
+        CK(k_->add_layernorm(x_, oxo, l.ln3, hb_, b, d, st_));
+        CK(lin_onto_bias(hb_, d, l.fc1, ofc1, ff, b, ff, d));
+        CK(k_->gelu(ofc1, (long)b * ff, st_));
+        CK(lin_onto_bias(ofc1, ff, l.fc2, ofc2, d, b, d, ff));
+        const Ln& next = i + 1 < nl ? dec_[i + 1].ln1 : dln_;
+        CK(k_->add_layernorm(x_, ofc2, next, hb_, b, d, st_));
+    }
+    // logits = hb emb^T (no bias), then the greedy choice and the position counter
+    if (b <= 8) {
+        int r = k_->gemv(hb_, d, emb_, logits_, dm_.vocab, b, dm_.vocab, d, nullptr, st_);
+        if (r == -1) return -1;
+        if (r == -2) CK(matmul(true, false, dm_.vocab, b, d, 1.f, emb_, d, 0, hb_, d, 0, 0.f, logits_, dm_.vocab, 0, 1));
+    } else {
+        CK(matmul(true, false, dm_.vocab, b, d, 1.f, emb_, d, 0, hb_, d, 0, 0.f, logits_, dm_.vocab, 0, 1));
+    }
+    const int bs1 = gc_.bs[0], bs2 = gc_.bs[1];
+    CK(k_->argmax_tok(logits_, dm_.vocab, sup_, tok_, done_, ctr_, b, mt, prompt_len, gc_.eos, bs1, bs2, st_));
+    return k_->advance(ctr_, st_);
+}
+
+int Engine::capture(int b, int prompt_len) {
+    if (graph_) {
+        cudaGraphExecDestroy(graph_);
+        graph_ = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    CUDA_CK(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
+    int r = step(b, prompt_len);
+    cudaError_t e = cudaStreamEndCapture(st_, &g);
+    if (r) {
+        if (g) cudaGraphDestroy(g);
+        return -1;
+    }
+    CUDA_CK(e);
+    e = cudaGraphInstantiate(&graph_, g, 0);
+    cudaGraphDestroy(g);
+    CUDA_CK(e);
+    CUDA_CK(cudaGraphUpload(graph_, st_));
+    graph_b_ = b;
+    graph_np_ = prompt_len;
+    return 0;
+}
+
+int Engine::replay() {
+    if (!graph_) return fail("replay: no captured step");
+    CUDA_CK(cudaGraphLaunch(graph_, st_));
+    return 0;
+}
+
+// transcribe.rs:104-167
+int Engine::transcribe(const float* mel, const int* frames, int n, const int* prompt, int np, int max_steps,
+                       bool graph, int threads, int* tokens, int* lens, float* times, double* stage_s) {
+    using clk = std::chrono::steady_clock;
+    const int mt = dm_.max_t, nm = dm_.n_mels, na = (int)gc_.align_heads.size();
+    if (n < 1 || n > bmax_) return fail("transcribe: 1..bmax clips per call");
+    if (max_steps < 1 || max_steps > mt - 1) max_steps = mt - 1;
+    auto t0 = clk::now();
+    // fp32 log-mel to the device, rounded to fp16 there (the reference rounds on the host with f2h, model.rs:549)
+    const size_t per = (size_t)nm * NFRAMES;
+    for (int g0 = 0; g0 < n; g0 += eg_) {
+        const int gn = std::min(eg_, n - g0);
+        CUDA_CK(cudaMemcpyAsync(mel32_, mel + per * g0, per * gn * 4, cudaMemcpyHostToDevice, st_));
+        CK(launch_f32_to_f16(mel32_, mel_, (long)(per * gn), st_));
+        CK(encode_dev(mel_, gn, g0));
+    }
+    CUDA_CK(cudaStreamSynchronize(st_));
+    auto t1 = clk::now();
+    std::vector<int> prompts((size_t)n * np);
+    for (int s = 0; s < n; s++) std::memcpy(&prompts[(size_t)s * np], prompt, np * 4);
+    CK(reset(prompts.data(), n, np));
+    if (graph && (graph_b_ != n || graph_np_ != np || !graph_)) CK(capture(n, np));
+    int steps = 0;
+    std::vector<int> dn(n);
+    while (steps < max_steps) {
+        if (graph) CK(replay());
+        else CK(step(n, np));
+        steps++;
+        if (steps % 8 == 0 && steps >= np) {
+            CUDA_CK(cudaMemcpyAsync(dn.data(), done_, (size_t)n * 4, cudaMemcpyDeviceToHost, st_));
+            CUDA_CK(cudaStreamSynchronize(st_));
+            bool all = true;
+            for (int v : dn) all = all && v != 0;
+            if (all) break;
+        }
+    }
+    CUDA_CK(cudaStreamSynchronize(st_));
+    graph_steps_ = steps;
+    auto t2 = clk::now();
+    CUDA_CK(cudaMemcpyAsync(tokens, tok_, (size_t)n * mt * 4, cudaMemcpyDeviceToHost, st_));
+    CUDA_CK(cudaStreamSynchronize(st_));
+    // the alignment rows of the generated tokens fed back as input; the last token takes the time of the one before
+    const size_t row = (size_t)na * TENC_;
+    std::vector<int> nseq(n), nrows(n);
+    size_t total = 0;
+    for (int s = 0; s < n; s++) {
+        const int* t = tokens + (size_t)s * mt;
+        int ns = std::min(steps + 1, mt);
+        for (int k = np; k < mt; k++)
+            if (t[k] == gc_.eos) {
+                ns = std::min(k + 1, mt);
+                break;
+            }
+        nseq[s] = ns;
+        nrows[s] = std::max(0, ns - 1 - np);
+        total += (size_t)nrows[s] * row;
+    }
+    std::vector<uint16_t> a16(total);
+    size_t off = 0;
+    for (int s = 0; s < n; s++) {
+        if (nrows[s] > 0)
+            CUDA_CK(cudaMemcpyAsync(a16.data() + off, (char*)align_ + 2 * ((size_t)s * mt + np) * row,
+                                    (size_t)nrows[s] * row * 2, cudaMemcpyDeviceToHost, st_));
+        off += (size_t)nrows[s] * row;
+    }
+    CUDA_CK(cudaStreamSynchronize(st_));
+    if (threads < 1) threads = (int)std::max(1u, std::thread::hardware_concurrency());
+    threads = std::min(threads, n);
+    std::vector<size_t> starts(n);
+    for (int s = 0, o = 0; s < n; s++) {
+        starts[s] = o;
+        o += nrows[s] * row;
+    }
+    auto work = [&](int w) {
+        std::vector<float> wf;
+        for (int s = w; s < n; s += threads) {
+            float* ts = times + (size_t)s * mt;
+            std::fill(ts, ts + mt, 0.f);
+            lens[s] = nseq[s];
+            const int rows = nrows[s];
+            if (rows <= 0) continue;
+            wf.resize((size_t)rows * row);
+            const uint16_t* src = a16.data() + starts[s];
+            for (size_t i = 0; i < wf.size(); i++) wf[i] = h2f(src[i]);
+            jump_times(wf.data(), rows, na, TENC_, frames[s] / 2, 7, ts + np);
+            ts[nseq[s] - 1] = ts[np + rows - 1];
+        }
+    };
+    std::vector<std::thread> th;
+    for (int w = 1; w < threads; w++) th.emplace_back(work, w);
+    work(0);
+    for (auto& t : th) t.join();
+    auto t3 = clk::now();
+    if (stage_s) {
+        stage_s[0] = std::chrono::duration<double>(t1 - t0).count();
+        stage_s[1] = std::chrono::duration<double>(t2 - t1).count();
+        stage_s[2] = std::chrono::duration<double>(t3 - t2).count();
+    }
+    return 0;
+}
+
+void* Engine::buffer(const std::string& name) const {
+    if (name == "tok") return tok_;
+    if (name == "done") return done_;
+    if (name == "ctr") return ctr_;
+    if (name == "align") return align_;
+    if (name == "logits") return logits_;
+    if (name == "eh") return eh_;
+    if (name == "eqkv") return eqkv_;
+    if (name == "eatt") return eatt_;
+    if (name == "xkv") return xkv_buf_;
+    if (name == "mel") return mel_;
+    if (name == "kc") return kc_;
+    if (name == "vc") return vc_;
+    if (name == "x") return x_;
+    if (name == "hb") return hb_;
+    if (name == "att") return att_;
+    if (name == "aslot") return aslot_;
+    return nullptr;
+}
+
+}  // namespace mmz

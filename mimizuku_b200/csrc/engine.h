@@ -1,0 +1,127 @@
+// The Whisper engine around the attention hot path: a C++ restatement of the reference's src/model.rs (Engine: weight
+// layout, buffers, encoder and decoder-step launch sequences) and src/transcribe.rs (batch driver with CUDA-graph
+// replay and token timestamps), with the GPU boundary of src/gpu.rs (launch by name, cuBLAS GEMM with the beta = 1
+// bias trick).
+//
+// The engine runs on one of two kernel images with the same buffer layouts:
+//   native     the sm_100a kernels of this library (the product)
+//   fatbin     any image that exports the reference's 23 kernel names with its argument lists (the reference's own
+//              kernels/whisper.cu build is one), launched by name with the reference's grid geometry (model.rs)
+#pragma once
+#include <cublas_v2.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <utility>
+#include <vector>
+
+namespace mmz {
+
+struct Dims {
+    int d, ff, nh, enc_layers, dec_layers, n_mels, vocab, max_t;
+};
+
+struct GenCfg {
+    int sot, eos, no_timestamps;
+    std::vector<int> suppress;
+    int bs[2];                                      // begin-suppressed tokens, -1 = none
+    std::vector<std::pair<int, int>> align_heads;   // (decoder layer, head)
+};
+
+struct Lin {
+    void* w;
+    void* b;
+};
+struct Ln {
+    void* w;
+    void* b;
+};
+
+class Kernels;
+
+class Engine {
+   public:
+    Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char* kernel_image, unsigned long long seed);
+    ~Engine();
+    bool ok() const { return err_.empty(); }
+    const std::string& error() const { return err_; }
+
+    // encoder for gn clips (fp16 log-mel on the device, [gn][n_mels][3000]); cross k/v into slots slot0..
+    int encode_dev(const void* mel16, int gn, int slot0);
+    // prompt tokens into each slot, all unfinished, position 0 (model.rs:627-637)
+    int reset(const int* prompts, int b, int np);
+    // one decoding step for b sequences (model.rs:648-736)
+    int step(int b, int prompt_len);
+    // captures step(b, prompt_len) as a CUDA graph (transcribe.rs:122-131) and replays it
+    int capture(int b, int prompt_len);
+    int replay();
+    // the whole pipeline for n <= bmax clips given host fp32 log-mel [n][n_mels][3000] (transcribe.rs:104-167):
+    // upload, encode in groups, greedy decoding (at most max_steps steps, stopping early when every sequence is done),
+    // then token timestamps on `threads` host threads. tokens [n][max_t], lens [n], times [n][max_t];
+    // stage_s = {encode, decode, timestamps} seconds
+    int transcribe(const float* mel, const int* frames, int n, const int* prompt, int np, int max_steps, bool graph,
+                   int threads, int* tokens, int* lens, float* times, double* stage_s);
+
+    void* buffer(const std::string& name) const;
+    cudaStream_t stream() const { return st_; }
+    const Dims& dims() const { return dm_; }
+    int bmax() const { return bmax_; }
+    int eg() const { return eg_; }
+    int na() const { return (int)gc_.align_heads.size(); }
+    size_t allocated() const { return allocated_; }
+    int graph_steps() const { return graph_steps_; }
+
+   private:
+    int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
+    int lin_onto_bias(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
+    int matmul(bool ta, bool tb, int m, int n, int k, float alpha, const void* a, int lda, long long sa, const void* b,
+               int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch);
+    void* alloc(size_t bytes);
+    void* dec_out(int layer, int which) const;
+    int init_weights(unsigned long long seed);
+
+    std::string err_;
+    Dims dm_;
+    GenCfg gc_;
+    int bmax_, eg_;
+    int dev_ = 0;
+    cudaStream_t st_ = nullptr;
+    cublasHandle_t blas_ = nullptr;
+    std::unique_ptr<Kernels> k_;
+    std::vector<void*> allocs_;
+    size_t allocated_ = 0;
+    cudaGraphExec_t graph_ = nullptr;
+    int graph_b_ = -1, graph_np_ = -1, graph_steps_ = 0;
+
+    // weights
+    struct EncLayer {
+        Ln ln1;
+        Lin qkv, o;
+        Ln ln2;
+        Lin fc1, fc2;
+    };
+    struct DecLayer {
+        Ln ln1;
+        Lin qkv, o;
+        Ln lnx;
+        Lin xq, xo;
+        Ln ln3;
+        Lin fc1, fc2;
+    };
+    std::vector<EncLayer> enc_;
+    std::vector<DecLayer> dec_;
+    Lin conv1_, conv2_, xkv_;
+    void *epos_, *emb_, *dpos_;
+    Ln eln_, dln_;
+    // encoder scratch for eg clips, decoder state for bmax sequences (model.rs:289-321)
+    void *mel_, *x1_, *h1_, *x2_, *ex_, *eh_, *eqkv_, *eatt_, *ef_;
+    void *xkv_buf_, *x_, *hb_, *att_, *dout_, *dbias_, *logits_, *kc_, *vc_, *s_, *stat_, *part_, *align_;
+    int *tok_, *done_, *ctr_, *aslot_;
+    unsigned char *sup_;
+    float* mel32_;
+    void* ws_;
+};
+
+}  // namespace mmz

@@ -1,0 +1,64 @@
+// Host-side helpers shared by the kernel launchers: per-device context (status word, wait limit, kernel attributes),
+// error recording, and TMA tensor-map encoding through the driver entry point (the library does not link libcuda).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mmz {
+
+struct DevCtx {
+    bool inited = false;
+    bool ok = false;
+    const char* err = "device context not initialised";
+    unsigned* status = nullptr;            // device address of the status word (4 x u32)
+    unsigned long long limit_ns = 1000000000ull;  // bound on every in-kernel wait
+    int sms = 0;
+};
+
+// context of the current device, initialised on first use (call mmz_init before any stream capture)
+DevCtx& dev_ctx();
+// records msg as the calling thread's last error and returns -1
+int fail(const char* msg);
+int failf(const char* fmt, ...);
+// the calling thread's last error message
+const char* last_error();
+// cudaGetLastError after a launch: 0 or fail
+int check_launch(const char* what);
+
+int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], const uint64_t strides[1],
+                 const uint32_t box[2], bool swizzle128);
+int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                 const uint32_t box[3], bool swizzle128);
+
+void init_dec_attn_attrs();
+void init_enc_attn_attrs();
+
+// launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
+int launch_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
+                      const int* done, int batch, int layer, int nl, int d, int na, int maxT, cudaStream_t st);
+int launch_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* ctr, const int* done, int batch,
+                     int maxT, int d, cudaStream_t st);
+int launch_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch, int maxT, int d, cudaStream_t st);
+int launch_enc_flash(const void* qkv, void* out, int groups, int d, cudaStream_t st);
+int launch_layernorm(const void* x, const void* w, const void* b, void* out, int rows, int dim, float eps,
+                     cudaStream_t st);
+int launch_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
+                         cudaStream_t st);
+
+// engine-side elementwise and token kernels (misc.cu)
+int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,
+                 cudaStream_t st);
+int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
+                      int batch, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st);
+int launch_advance(int* ctr, cudaStream_t st);
+int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st);
+int launch_im2col2(const void* h1, void* X, long n, int d, cudaStream_t st);
+int launch_gelu(void* x, long n, cudaStream_t st);
+int launch_add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st);
+int launch_fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st);
+int launch_fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st);
+int launch_fill_normal(void* p, long n, unsigned long long seed, float mean, float std, cudaStream_t st);
+int launch_f32_to_f16(const float* src, void* dst, long n, cudaStream_t st);
+
+}  // namespace mmz

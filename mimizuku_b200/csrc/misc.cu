@@ -1,0 +1,215 @@
+// The engine's elementwise and token kernels around the attention path: the encoder stem helpers, the decoder
+// embedding, the greedy token choice and the position counter, plus the harness's seeded weight initialiser.
+// They compute what the reference engine's kernels of the same names compute (kernels/whisper.cu:92-139, 303-307,
+// 451-495), with 16-byte accesses where the layout allows.
+#include "common.cuh"
+#include "launch.h"
+
+namespace mmz {
+
+static inline unsigned blocks(long n, int per) { return (unsigned)((n + per - 1) / per); }
+
+// x[b] = h(tok_emb[tok[b, p]] + pos_emb[p]), p = ctr[0] (kernels/whisper.cu:303-307)
+__global__ void embed_kernel(const int* __restrict__ tok, const int* __restrict__ ctr, const h16* __restrict__ emb,
+                             const h16* __restrict__ pe, h16* __restrict__ x, int maxT, int d) {
+    const int b = blockIdx.x, p = ctr[0], t = tok[b * maxT + p];
+    for (int c = threadIdx.x; c < d / 2; c += blockDim.x) {
+        float2 e = __half22float2(reinterpret_cast<const __half2*>(emb + (long)t * d)[c]);
+        float2 q = __half22float2(reinterpret_cast<const __half2*>(pe + (long)p * d)[c]);
+        reinterpret_cast<__half2*>(x + (long)b * d)[c] = __floats2half2_rn(e.x + q.x, e.y + q.y);
+    }
+}
+
+// Greedy choice of token p + 1 (kernels/whisper.cu:451-493): suppressed ids (sup[i] != 0, and bs1 / bs2 at the first
+// generated position) are skipped, ties go to the lower id, prompt positions stay, finished rows and rows with every
+// id suppressed get eos.
+__global__ void __launch_bounds__(512) argmax_kernel(const h16* __restrict__ logits, int V, const unsigned char* sup,
+                                                     int* tok, int* done, const int* ctr, int maxT, int prompt_len,
+                                                     int eos, int bs1, int bs2) {
+    __shared__ float sv[16];
+    __shared__ int si[16];
+    const int b = blockIdx.x, p = ctr[0];
+    if (p + 1 < prompt_len || p + 1 >= maxT) return;
+    const bool first = p + 1 == prompt_len;
+    const h16* lg = logits + (long)b * V;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        if (sup[i] || (first && (i == bs1 || i == bs2))) continue;
+        const float v = f(lg[i]);
+        if (v > best || (v == best && i < bi)) {
+            best = v;
+            bi = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffff, best, o);
+        const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        best = l < nw ? sv[l] : -INFINITY;
+        bi = l < nw ? si[l] : 0x7fffffff;
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffff, best, o);
+            const int oi = __shfl_xor_sync(0xffffffff, bi, o);
+            if (ov > best || (ov == best && oi < bi)) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (l == 0) {
+            const int t = (done[b] || bi == 0x7fffffff) ? eos : bi;
+            tok[b * maxT + p + 1] = t;
+            if (t == eos) done[b] = 1;
+        }
+    }
+}
+
+__global__ void advance_kernel(int* ctr) { ctr[0] += 1; }
+
+// conv1 as a GEMM operand: X[g, t, ci * 3 + k] = mel[g, ci, t + k - 1] (kernels/whisper.cu:121-129)
+__global__ void im2col1_kernel(const h16* __restrict__ mel, h16* __restrict__ X, long n, int nm) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int j = (int)(i % (3 * nm));
+    const long r = i / (3 * nm);
+    const int t = (int)(r % NFR), g = (int)(r / NFR), ci = j / 3, tt = t + j % 3 - 1;
+    X[i] = (tt >= 0 && tt < NFR) ? mel[((long)g * nm + ci) * NFR + tt] : h(0.f);
+}
+
+// conv2 (stride 2) as a GEMM operand: X[g, t, ci * 3 + k] = h1[g, 2t + k - 1, ci] (kernels/whisper.cu:131-139)
+__global__ void im2col2_kernel(const h16* __restrict__ h1, h16* __restrict__ X, long n, int d) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int j = (int)(i % (3 * d));
+    const long r = i / (3 * d);
+    const int t = (int)(r % TENC), g = (int)(r / TENC), ci = j / 3, tt = 2 * t + j % 3 - 1;
+    X[i] = (tt >= 0 && tt < NFR) ? h1[((long)g * NFR + tt) * d + ci] : h(0.f);
+}
+
+// exact (erf) GELU over half2 pairs (kernels/whisper.cu:106-113)
+__device__ __forceinline__ float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
+__global__ void gelu_kernel(__half2* x, long n2) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n2) return;
+    const float2 v = __half22float2(x[i]);
+    x[i] = __floats2half2_rn(gelu(v.x), gelu(v.y));
+}
+
+// x[r, c] += pos[r % period, c] (kernels/whisper.cu:115-119)
+__global__ void add_pos_kernel(h16* x, const h16* __restrict__ pos, long rows, int n, int period) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * n) return;
+    const long r = i / n;
+    const int c = (int)(i % n);
+    x[i] = h(f(x[i]) + f(pos[(r % period) * n + c]));
+}
+
+// rows of an output with row stride ld <- bias (kernels/whisper.cu:92-97), 8 halves per thread
+__global__ void fill_bias_kernel(h16* y, const h16* __restrict__ bias, long rows, int n, long ld) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x, n8 = n / 8;
+    if (i >= rows * n8) return;
+    const long r = i / n8;
+    const int c = (int)(i % n8);
+    reinterpret_cast<uint4*>(y + r * ld)[c] = reinterpret_cast<const uint4*>(bias)[c];
+}
+
+// bias of the head-contiguous cross k/v buffer: y[blk, j, c] = bias[blk * 64 + c] (kernels/whisper.cu:99-104)
+__global__ void fill_bias_heads_kernel(h16* y, const h16* __restrict__ bias, long n8) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n8) return;
+    reinterpret_cast<uint4*>(y)[i] =
+        reinterpret_cast<const uint4*>(bias)[(i / ((long)TENC * HD / 8)) * (HD / 8) + i % (HD / 8)];
+}
+
+// seeded N(mean, std) in fp16: splitmix64 of (seed, index) -> two uniforms -> Box-Muller
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+__global__ void fill_normal_kernel(h16* p, long n, unsigned long long seed, float mean, float std) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const uint64_t r = splitmix64(seed * 0x2545f4914f6cdd1dull + (uint64_t)i);
+    const float u1 = ((uint32_t)(r >> 40) + 0.5f) * (1.f / 16777216.f);
+    const float u2 = (uint32_t)(r & 0xffffff) * (1.f / 16777216.f);
+    const float z = sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+    p[i] = h(mean + std * z);
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ src, h16* __restrict__ dst, long n) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = h(src[i]);
+}
+
+int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,
+                 cudaStream_t st) {
+    embed_kernel<<<batch, 128, 0, st>>>(tok, ctr, (const h16*)emb, (const h16*)pe, (h16*)x, maxT, d);
+    return check_launch("embed");
+}
+
+int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
+                      int batch, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) {
+    argmax_kernel<<<batch, 512, 0, st>>>((const h16*)logits, V, sup, tok, done, ctr, maxT, prompt_len, eos, bs1, bs2);
+    return check_launch("argmax_tok");
+}
+
+int launch_advance(int* ctr, cudaStream_t st) {
+    advance_kernel<<<1, 1, 0, st>>>(ctr);
+    return check_launch("advance");
+}
+
+int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) {
+    im2col1_kernel<<<blocks(n, 256), 256, 0, st>>>((const h16*)mel, (h16*)X, n, nm);
+    return check_launch("im2col1");
+}
+
+int launch_im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) {
+    im2col2_kernel<<<blocks(n, 256), 256, 0, st>>>((const h16*)h1, (h16*)X, n, d);
+    return check_launch("im2col2");
+}
+
+int launch_gelu(void* x, long n, cudaStream_t st) {
+    gelu_kernel<<<blocks(n / 2, 256), 256, 0, st>>>((__half2*)x, n / 2);
+    return check_launch("gelu");
+}
+
+int launch_add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) {
+    add_pos_kernel<<<blocks(rows * n, 256), 256, 0, st>>>((h16*)x, (const h16*)pos, rows, n, period);
+    return check_launch("add_pos");
+}
+
+int launch_fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st) {
+    fill_bias_kernel<<<blocks(rows * (n / 8), 256), 256, 0, st>>>((h16*)y, (const h16*)bias, rows, n, ld);
+    return check_launch("fill_bias");
+}
+
+int launch_fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) {
+    fill_bias_heads_kernel<<<blocks(n8, 256), 256, 0, st>>>((h16*)y, (const h16*)bias, n8);
+    return check_launch("fill_bias_heads");
+}
+
+int launch_fill_normal(void* p, long n, unsigned long long seed, float mean, float std, cudaStream_t st) {
+    fill_normal_kernel<<<blocks(n, 256), 256, 0, st>>>((h16*)p, n, seed, mean, std);
+    return check_launch("fill_normal");
+}
+
+int launch_f32_to_f16(const float* src, void* dst, long n, cudaStream_t st) {
+    f32_to_f16_kernel<<<blocks(n, 256), 256, 0, st>>>(src, (h16*)dst, n);
+    return check_launch("f32_to_f16");
+}
+
+}  // namespace mmz

@@ -1,0 +1,121 @@
+// Per-device runtime state of the library: the status word every bounded wait reports into, kernel attributes,
+// the calling thread's last error, and tensor-map encoding through the driver entry point.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace mmz {
+
+__device__ unsigned g_status[4];
+
+static thread_local std::string t_err;
+
+int fail(const char* msg) {
+    t_err = msg ? msg : "error";
+    return -1;
+}
+
+int failf(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    return fail(buf);
+}
+
+const char* last_error() { return t_err.c_str(); }
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return failf("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return 0;
+}
+
+static std::mutex g_mu;
+static DevCtx g_ctx[64];
+
+DevCtx& dev_ctx() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        static DevCtx bad;
+        bad.ok = false;
+        bad.err = "no CUDA device";
+        return bad;
+    }
+    DevCtx& c = g_ctx[dev];
+    if (c.inited) return c;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (c.inited) return c;
+    c.inited = true;
+    c.ok = false;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+        c.err = "cudaGetDeviceProperties failed";
+        return c;
+    }
+    if (prop.major != 10 || prop.minor != 0) {
+        c.err = "the mimizuku_b200 kernels are built for sm_100a (B200) only";
+        return c;
+    }
+    c.sms = prop.multiProcessorCount;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) {
+        c.err = "cudaGetSymbolAddress(status) failed";
+        return c;
+    }
+    c.status = (unsigned*)p;
+    if (const char* s = getenv("MMZ_WAIT_LIMIT_MS")) c.limit_ns = (unsigned long long)atoll(s) * 1000000ull;
+    init_dec_attn_attrs();
+    init_enc_attn_attrs();
+    cudaGetLastError();
+    c.ok = true;
+    c.err = "";
+    return c;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+
+static int make_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* dims, const uint64_t* strides,
+                     const uint32_t* box, bool swizzle128) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return -1;
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), (const cuuint64_t*)dims,
+                    (const cuuint64_t*)strides, (const cuuint32_t*)box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -1;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], const uint64_t strides[1],
+                 const uint32_t box[2], bool swizzle128) {
+    return make_tmap(map, 2, base, dims, strides, box, swizzle128);
+}
+
+int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
+                 const uint32_t box[3], bool swizzle128) {
+    return make_tmap(map, 3, base, dims, strides, box, swizzle128);
+}
+
+}  // namespace mmz
