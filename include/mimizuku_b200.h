@@ -60,11 +60,17 @@ int mmz_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch,
 /* Decoder cross-attention of one layer over the 1500 encoder positions: q [batch][d] (the xq projection), kv the
  * head-contiguous cross k/v buffer [batch][nl][k|v][heads][1500][64], out [batch][d]. For the heads with
  * aslot[layer * heads + head] = s >= 0, the fp16 probabilities are also stored into align[b][ctr[0]][s][1500]
- * (align is [batch][max_t][na][1500]). Sequences with done[b] != 0 are skipped. One fused launch replaces
- * cross_scores + cross_pv + cross_combine (kernels/whisper.cu:368, :407, :443; src/model.rs:676-705) and needs none
- * of their S / stat / part scratch. kv 16-byte aligned. */
+ * (align is [batch][max_t][na][1500]). Sequences with done[b] != 0 are skipped.
+ * Two streaming split-KV kernels (scores and 64-position chunk statistics; then probabilities, P.V and the in-order
+ * combine of the 24 chunk partials by the last CTA of each (sequence, head)), the second a programmatic dependent
+ * launch of the first. Replaces cross_scores + cross_pv + cross_combine (kernels/whisper.cu:368, :407, :443;
+ * src/model.rs:676-705), whose S / stat / part buffers (model.rs:452-454) become `scratch`: a device buffer of at
+ * least mmz_cross_attn_scratch_bytes(batch, d) bytes, 16-byte aligned and zeroed once before its first use (the kernels
+ * leave it reusable). Launches that share a scratch buffer must not overlap on the GPU. kv 16-byte aligned. */
 int mmz_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
-                   const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* stream);
+                   const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* scratch,
+                   unsigned long long scratch_bytes, void* stream);
+unsigned long long mmz_cross_attn_scratch_bytes(int batch, int d);
 
 /* out = layernorm(x) per row of `dim` (even, <= 2048) fp16 values, fp32 statistics, eps as given.
  * Replaces layernorm (kernels/whisper.cu:66; src/model.rs:529-531). */
@@ -144,6 +150,9 @@ void* mmz_engine_stream(mmz_engine* e);
 int mmz_engine_sync(mmz_engine* e);
 /* Device bytes the engine allocated. */
 long long mmz_engine_allocated(mmz_engine* e);
+/* Kernels of the engine's kernel image launched so far (each graph replay counts every kernel of the captured step;
+ * cuBLAS GEMMs are not counted). */
+long long mmz_engine_launches(mmz_engine* e);
 
 #ifdef __cplusplus
 }

@@ -1,12 +1,13 @@
 """mimizuku_b200: the B200-native attention hot path of the mimizuku Whisper engine.
 
 The product is the C-ABI library ``libmimizuku_b200.so`` (declared in ``include/mimizuku_b200.h``): sm_100a kernels
-for encoder flash attention (tcgen05/TMEM/TMA), decoder self- and cross-attention (cluster split-KV), fused
+for encoder flash attention (tcgen05/TMEM/TMA), decoder self-attention (TMA-streamed) and cross-attention (split-KV
+streaming kernels), fused
 residual-add + LayerNorm, the engine that drives them (a C++ restatement of the reference's model.rs and
 transcribe.rs) and the CPU timestamp stage (align.rs). This module binds it with ctypes under the reference's names
 (``enc_flash``, ``self_attn``, ``cross_attn``, ``layernorm``, ``add_layernorm``, ``jump_times``, ``dtw``, ``Engine``).
 
-Importing fails loudly when the library has not been built (``python -m mimizuku_b200.build``): there is no CPU or
+Importing fails loudly when the library has not been built (``python mimizuku_b200/build.py``): there is no CPU or
 Python fallback for any of these functions.
 """
 import ctypes
@@ -18,7 +19,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmimizuku_b200.so")
 
 if not os.path.exists(LIB_PATH):
-    raise ImportError(f"{LIB_PATH} is missing; build it with `python -m mimizuku_b200.build`")
+    raise ImportError(f"{LIB_PATH} is missing; build it with `python mimizuku_b200/build.py`")
 
 lib = ctypes.CDLL(LIB_PATH)
 
@@ -54,7 +55,8 @@ SIGNATURES = {
     "mmz_enc_flash": (_I, [_P, _P, _I, _I, _P]),
     "mmz_self_attn": (_I, [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P]),
     "mmz_kv_write": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
-    "mmz_cross_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "mmz_cross_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _ULL, _P]),
+    "mmz_cross_attn_scratch_bytes": (_ULL, [_I, _I]),
     "mmz_layernorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _P]),
     "mmz_add_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _I, _F, _P]),
     "mmz_jump_times": (_I, [_FP, _I, _I, _I, _I, _I, _FP]),
@@ -75,6 +77,7 @@ SIGNATURES = {
     "mmz_engine_stream": (_P, [_P]),
     "mmz_engine_sync": (_I, [_P]),
     "mmz_engine_allocated": (_LL, [_P]),
+    "mmz_engine_launches": (_LL, [_P]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():
@@ -158,11 +161,21 @@ def kv_write(qkv, kc, vc, ctr, max_t, d, batch, stream=None):
     _check(lib.mmz_kv_write(_ptr(qkv), _ptr(kc), _ptr(vc), _ptr(ctr), batch, max_t, d, _stream(stream)), "kv_write")
 
 
-def cross_attn(q, kv, out, align, aslot, ctr, done, layer, nl, d, na, max_t, batch=None, stream=None):
-    """kernels/whisper.cu:368-449 cross_scores + cross_pv + cross_combine (fused)."""
+def cross_attn_scratch_bytes(batch, d):
+    """Bytes of device scratch mmz_cross_attn needs for `batch` sequences of width d."""
+    return lib.mmz_cross_attn_scratch_bytes(batch, d)
+
+
+def cross_attn(q, kv, out, align, aslot, ctr, done, layer, nl, d, na, max_t, scratch, batch=None, stream=None,
+               scratch_bytes=None):
+    """kernels/whisper.cu:368-449 cross_scores + cross_pv + cross_combine as two streaming kernels. scratch: a
+    zeroed device buffer (torch tensor or address) of at least cross_attn_scratch_bytes(batch, d) bytes."""
     b = batch if batch is not None else done.shape[0]
-    _check(lib.mmz_cross_attn(_ptr(q), _ptr(kv), _ptr(out), _ptr(align), _ptr(aslot), _ptr(ctr), _ptr(done), b, layer,
-                              nl, d, na, max_t, _stream(stream)), "cross_attn")
+    if scratch_bytes is None:
+        scratch_bytes = (scratch.numel() * scratch.element_size() if hasattr(scratch, "numel")
+                         else cross_attn_scratch_bytes(b, d))
+    _check(lib.mmz_cross_attn(_ptr(q), _ptr(kv), _ptr(out), _ptr(align), _ptr(aslot), _ptr(ctr), _ptr(done), b,
+                              layer, nl, d, na, max_t, _ptr(scratch), scratch_bytes, _stream(stream)), "cross_attn")
 
 
 def layernorm(x, w, b, out, eps=1e-5, rows=None, stream=None):

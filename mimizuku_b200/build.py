@@ -1,7 +1,7 @@
 """Builds libmimizuku_b200.so in-tree: the sm_100a kernels (nvcc, -gencode arch=compute_100a,code=sm_100a), the C++
 engine and CPU stages, linked against cuBLAS with a static CUDA runtime.
 
-    python -m mimizuku_b200.build [--force] [-j N]
+    python mimizuku_b200/build.py [--force] [-j N]      (by path: importing the package needs the library)
 
 Objects go to mimizuku_b200/_build/; a source is recompiled when it or a header changed.
 """

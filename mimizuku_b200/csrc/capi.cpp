@@ -67,8 +67,14 @@ int mmz_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch,
 }
 
 int mmz_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
-                   const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* stream) {
-    return launch_cross_attn(q, kv, out, align, aslot, ctr, done, batch, layer, nl, d, na, max_t, S(stream));
+                   const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* scratch,
+                   unsigned long long scratch_bytes, void* stream) {
+    return launch_cross_attn(q, kv, out, align, aslot, ctr, done, batch, layer, nl, d, na, max_t, scratch,
+                             (size_t)scratch_bytes, S(stream));
+}
+
+unsigned long long mmz_cross_attn_scratch_bytes(int batch, int d) {
+    return batch < 1 || d < 64 ? 0 : (unsigned long long)cross_attn_scratch_bytes(batch, d);
 }
 
 int mmz_layernorm(const void* x, const void* w, const void* b, void* out, int rows, int dim, float eps, void* stream) {
@@ -179,5 +185,6 @@ int mmz_engine_sync(mmz_engine* e) {
     return r == cudaSuccess ? 0 : failf("engine stream: %s", cudaGetErrorString(r));
 }
 long long mmz_engine_allocated(mmz_engine* e) { return e ? (long long)e->e->allocated() : 0; }
+long long mmz_engine_launches(mmz_engine* e) { return e ? e->e->launches() : 0; }
 
 }  // extern "C"

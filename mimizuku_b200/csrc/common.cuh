@@ -80,6 +80,48 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Wait with cluster-scope acquire: pairs with remote arrivals that release stores made into this CTA's shared memory
+// by other CTAs of the cluster. Bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                  uint64_t limit_ns, unsigned* status, unsigned kernel,
+                                                  unsigned where) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    uint64_t t0 = globaltimer();
+    for (;;) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (abort && *abort) return false;
+        if (globaltimer() - t0 > limit_ns) {
+            if (abort) *abort = 1;
+            report(status, ST_TIMEOUT, kernel, where);
+            return false;
+        }
+    }
+}
+// arrive on the mbarrier at `remote` (a shared::cluster address from dsmem_addr), releasing this thread's earlier
+// stores to the cluster
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+// orders this thread's earlier stores (shared::cluster included) at cluster scope, before a CTA barrier after which
+// one thread signals them with a remote arrival
+__device__ __forceinline__ void fence_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem_f32x2(uint32_t addr, float2 v) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+
 // ---------------------------------------------------------------- bulk / tensor copies (global -> shared)
 
 // contiguous copy; dst, src 16-byte aligned and bytes a multiple of 16

@@ -26,6 +26,7 @@ constexpr size_t WS_BYTES = 64u << 20;  // fixed cuBLAS workspace: no allocation
 
 class Kernels {
    public:
+    long long launches = 0;  // kernels of this image launched (or replayed) so far
     virtual ~Kernels() {}
     virtual bool native() const = 0;
     virtual int layernorm(const void* x, const Ln& l, void* y, int rows, int d, cudaStream_t st) = 0;
@@ -56,51 +57,55 @@ class Kernels {
 
 class NativeKernels : public Kernels {
    public:
+    void* xscratch = nullptr;  // cross-attention scratch (the reference's S / stat / part, model.rs:452-454)
+    size_t xscratch_bytes = 0;
     bool native() const override { return true; }
     int layernorm(const void* x, const Ln& l, void* y, int rows, int d, cudaStream_t st) override {
-        return launch_layernorm(x, l.w, l.b, y, rows, d, EPS, st);
+        return ++launches, launch_layernorm(x, l.w, l.b, y, rows, d, EPS, st);
     }
     int add_layernorm(void* x, const void* dx, const Ln& l, void* y, int rows, int d, cudaStream_t st) override {
-        return launch_add_layernorm(x, dx, l.w, l.b, y, rows, d, EPS, st);
+        return ++launches, launch_add_layernorm(x, dx, l.w, l.b, y, rows, d, EPS, st);
     }
     int enc_attn(const void* qkv, void* out, int gn, int d, int, cudaStream_t st) override {
-        return launch_enc_flash(qkv, out, gn, d, st);
+        return ++launches, launch_enc_flash(qkv, out, gn, d, st);
     }
     // kv_write is folded into the self-attention kernel
     int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b, int maxT,
                   int d, int, cudaStream_t st) override {
-        return launch_self_attn(qkv, kc, vc, att, ctr, done, b, maxT, d, st);
+        return ++launches, launch_self_attn(qkv, kc, vc, att, ctr, done, b, maxT, d, st);
     }
-    // one fused kernel; the reference's S / stat / part scratch is not needed
+    // two streaming kernels joined by a programmatic dependent launch, on the engine's cross-attention scratch
     int cross_attn(const void* xq, const void* kv, void*, void*, void*, void* att, void* align, const int* aslot,
                    const int* ctr, const int* done, int b, int layer, int nl, int d, int, int na, int maxT,
                    cudaStream_t st) override {
-        return launch_cross_attn(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, st);
+        launches += 2;
+        return launch_cross_attn(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, xscratch,
+                                 xscratch_bytes, st);
     }
     int embed(const int* tok, const int* ctr, const void* emb, const void* dpos, void* x, int b, int maxT, int d,
               cudaStream_t st) override {
-        return launch_embed(tok, ctr, emb, dpos, x, b, maxT, d, st);
+        return ++launches, launch_embed(tok, ctr, emb, dpos, x, b, maxT, d, st);
     }
     int argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr, int b,
                    int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) override {
-        return launch_argmax_tok(logits, V, sup, tok, done, ctr, b, maxT, prompt_len, eos, bs1, bs2, st);
+        return ++launches, launch_argmax_tok(logits, V, sup, tok, done, ctr, b, maxT, prompt_len, eos, bs1, bs2, st);
     }
-    int advance(int* ctr, cudaStream_t st) override { return launch_advance(ctr, st); }
+    int advance(int* ctr, cudaStream_t st) override { return ++launches, launch_advance(ctr, st); }
     int im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) override {
-        return launch_im2col1(mel, X, n, nm, st);
+        return ++launches, launch_im2col1(mel, X, n, nm, st);
     }
     int im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) override {
-        return launch_im2col2(h1, X, n, d, st);
+        return ++launches, launch_im2col2(h1, X, n, d, st);
     }
-    int gelu(void* x, long n, cudaStream_t st) override { return launch_gelu(x, n, st); }
+    int gelu(void* x, long n, cudaStream_t st) override { return ++launches, launch_gelu(x, n, st); }
     int add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) override {
-        return launch_add_pos(x, pos, rows, n, period, st);
+        return ++launches, launch_add_pos(x, pos, rows, n, period, st);
     }
     int fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st) override {
-        return launch_fill_bias(y, bias, rows, n, ld, st);
+        return ++launches, launch_fill_bias(y, bias, rows, n, ld, st);
     }
     int fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) override {
-        return launch_fill_bias_heads(y, bias, n8, st);
+        return ++launches, launch_fill_bias_heads(y, bias, n8, st);
     }
     int gemv(const void*, int, const void*, void*, int, int, int, int, const void*, cudaStream_t) override { return -2; }
 };
@@ -187,6 +192,7 @@ class FatbinKernels : public Kernels {
         std::vector<void*> ptrs;
         for (auto& a : vals) ptrs.push_back(&a.v);
         CUresult r = launch_(fn, gx, gy, gz, block, 1, 1, smem, (CUstream)st, ptrs.data(), nullptr);
+        ++launches;
         return r == CUDA_SUCCESS ? 0 : failf("%s: cuLaunchKernel failed (%d)", name, (int)r);
     }
     // elementwise launch over n items (gpu.rs:203-206)
@@ -379,11 +385,15 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         s_ = alloc(b * nh * TENC_ * 4);
         stat_ = alloc(b * nh * NCH * 8);
         part_ = alloc(b * nh * NCH * HDIM * 4);
-    } else {
-        s_ = stat_ = part_ = nullptr;
+    } else {  // the native kernels' scratch for the same role (zero-filled, as the kernels require)
+        NativeKernels* nk = static_cast<NativeKernels*>(k_.get());
+        nk->xscratch_bytes = cross_attn_scratch_bytes(bmax, d);
+        nk->xscratch = alloc(nk->xscratch_bytes);
+        s_ = nk->xscratch;
+        stat_ = part_ = nullptr;
     }
     align_ = H(b * mt * na * TENC_);
-    for (void* p : {mel_, (void*)mel32_, x1_, h1_, x2_, ex_, eh_, eqkv_, eatt_, ef_, xkv_buf_, (void*)tok_, (void*)done_, (void*)ctr_,
+    for (void* p : {s_, mel_, (void*)mel32_, x1_, h1_, x2_, ex_, eh_, eqkv_, eatt_, ef_, xkv_buf_, (void*)tok_, (void*)done_, (void*)ctr_,
                     x_, hb_, att_, dout_, dbias_, logits_, kc_, vc_, align_})
         if (!p) {
             err_ = "device memory allocation failed";
@@ -614,7 +624,10 @@ int Engine::capture(int b, int prompt_len) {
     }
     cudaGraph_t g = nullptr;
     CUDA_CK(cudaStreamBeginCapture(st_, cudaStreamCaptureModeThreadLocal));
+    const long long before = k_->launches;
     int r = step(b, prompt_len);
+    step_launches_ = k_->launches - before;
+    k_->launches = before;  // captured, not executed
     cudaError_t e = cudaStreamEndCapture(st_, &g);
     if (r) {
         if (g) cudaGraphDestroy(g);
@@ -633,6 +646,7 @@ int Engine::capture(int b, int prompt_len) {
 int Engine::replay() {
     if (!graph_) return fail("replay: no captured step");
     CUDA_CK(cudaGraphLaunch(graph_, st_));
+    k_->launches += step_launches_;
     return 0;
 }
 
@@ -736,6 +750,8 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
     }
     return 0;
 }
+
+long long Engine::launches() const { return k_ ? k_->launches : 0; }
 
 void* Engine::buffer(const std::string& name) const {
     if (name == "tok") return tok_;

@@ -72,6 +72,10 @@ class Engine {
     int na() const { return (int)gc_.align_heads.size(); }
     size_t allocated() const { return allocated_; }
     int graph_steps() const { return graph_steps_; }
+    // kernels of the engine's kernel image launched so far (graph replays count every kernel of the step; cuBLAS
+    // GEMMs are not counted)
+    long long launches() const;
+    long long step_launches() const { return step_launches_; }
 
    private:
     int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
@@ -94,6 +98,7 @@ class Engine {
     size_t allocated_ = 0;
     cudaGraphExec_t graph_ = nullptr;
     int graph_b_ = -1, graph_np_ = -1, graph_steps_ = 0;
+    long long step_launches_ = 0;
 
     // weights
     struct EncLayer {

@@ -4,6 +4,8 @@
 //
 // Compiled with -ffp-contract=off: the reference's f32 arithmetic is never fused, and the DTW path must come out
 // bit-identical.
+#include <immintrin.h>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -110,31 +112,116 @@ static inline int32_t total_key(float x) {
     return k ^ (int32_t)(((uint32_t)(k >> 31)) >> 1);
 }
 
+static inline void cx(int32_t& a, int32_t& b) {
+    const int32_t lo = a < b ? a : b, hi = a < b ? b : a;
+    a = lo;
+    b = hi;
+}
+
+// median of 7 keys: a 16-comparator sorting network (checked on every 0-1 input), branch-free
+static inline int32_t median7(int32_t a0, int32_t a1, int32_t a2, int32_t a3, int32_t a4, int32_t a5, int32_t a6) {
+    cx(a0, a6); cx(a2, a3); cx(a4, a5);
+    cx(a0, a2); cx(a1, a4); cx(a3, a6);
+    cx(a0, a1); cx(a2, a5); cx(a3, a4);
+    cx(a1, a2); cx(a4, a6);
+    cx(a2, a3); cx(a4, a5);
+    cx(a1, a2); cx(a3, a4); cx(a5, a6);
+    return a3;
+}
+
+// width-7 median filter of one row of keys with reflect padding; the interior loop has no branches
+__attribute__((target("avx2"))) static void median7_row_avx2(const int32_t* k, int cols, int32_t* med) {
+    for (int j = 3; j < cols - 3; j++) med[j] = median7(k[j - 3], k[j - 2], k[j - 1], k[j], k[j + 1], k[j + 2], k[j + 3]);
+}
+static void median7_row_plain(const int32_t* k, int cols, int32_t* med) {
+    for (int j = 3; j < cols - 3; j++) med[j] = median7(k[j - 3], k[j - 2], k[j - 1], k[j], k[j + 1], k[j + 2], k[j + 3]);
+}
+
+static inline float key_to_f(int32_t k) {
+    k ^= (int32_t)(((uint32_t)(k >> 31)) >> 1);  // the key map is its own inverse
+    float v;
+    std::memcpy(&v, &k, 4);
+    return v;
+}
+
+// z-scores of one head: z[i][j] = rh(rh(w[i][j] - rh(mean_j)) / rh(std_j)), 0 where std_j = 0 (src/align.rs:16-25).
+// Column statistics accumulate over the rows in order, exactly as the reference's per-column sums do.
+static void zscore_plain(const float* w, int rows, int heads, int a, int cols_full, int cols, float* z, float* mean,
+                         float* sd, int j0 = 0) {
+    auto at = [&](int i, int j) { return w[((long)i * heads + a) * cols_full + j]; };
+    for (int j = j0; j < cols; j++) {
+        float sum = -0.0f;  // Rust's f32 Sum starts from -0.0
+        for (int i = 0; i < rows; i++) sum += at(i, j);
+        const float mean_f = sum / (float)rows;
+        float vs = -0.0f;
+        for (int i = 0; i < rows; i++) {
+            const float t = at(i, j) - mean_f;
+            vs += t * t;
+        }
+        mean[j] = rh(mean_f);
+        sd[j] = rh(std::sqrt(vs / (float)rows));
+        // a constant column (always so for a single row) scores 0 (src/align.rs:22-23)
+        for (int i = 0; i < rows; i++) z[(long)i * cols + j] = sd[j] > 0.f ? rh(rh(at(i, j) - mean[j]) / sd[j]) : 0.f;
+    }
+}
+
+// The same with 8 columns per AVX2 lane group and the hardware's round-to-nearest-even fp16 conversion, which equals
+// f2h / h2f for every finite value (the caller takes the plain path when the input holds a non-finite value).
+__attribute__((target("avx2,f16c"))) static inline __m256 rh8(__m256 x) {
+    return _mm256_cvtph_ps(_mm256_cvtps_ph(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
+}
+__attribute__((target("avx2,f16c"))) static void zscore_avx2(const float* w, int rows, int heads, int a,
+                                                             int cols_full, int cols, float* z, float* mean,
+                                                             float* sd, float* acc) {
+    const int c8 = cols / 8 * 8;
+    const __m256 rows_f = _mm256_set1_ps((float)rows), zero = _mm256_setzero_ps();
+    for (int j = 0; j < c8; j += 8) _mm256_storeu_ps(acc + j, _mm256_set1_ps(-0.0f));
+    for (int i = 0; i < rows; i++) {
+        const float* r = w + ((long)i * heads + a) * cols_full;
+        for (int j = 0; j < c8; j += 8) _mm256_storeu_ps(acc + j, _mm256_add_ps(_mm256_loadu_ps(acc + j), _mm256_loadu_ps(r + j)));
+    }
+    for (int j = 0; j < c8; j += 8) _mm256_storeu_ps(mean + j, _mm256_div_ps(_mm256_loadu_ps(acc + j), rows_f));
+    for (int j = 0; j < c8; j += 8) _mm256_storeu_ps(acc + j, _mm256_set1_ps(-0.0f));
+    for (int i = 0; i < rows; i++) {
+        const float* r = w + ((long)i * heads + a) * cols_full;
+        for (int j = 0; j < c8; j += 8) {
+            const __m256 t = _mm256_sub_ps(_mm256_loadu_ps(r + j), _mm256_loadu_ps(mean + j));
+            _mm256_storeu_ps(acc + j, _mm256_add_ps(_mm256_loadu_ps(acc + j), _mm256_mul_ps(t, t)));
+        }
+    }
+    for (int j = 0; j < c8; j += 8) {
+        _mm256_storeu_ps(sd + j, rh8(_mm256_sqrt_ps(_mm256_div_ps(_mm256_loadu_ps(acc + j), rows_f))));
+        _mm256_storeu_ps(mean + j, rh8(_mm256_loadu_ps(mean + j)));
+    }
+    for (int i = 0; i < rows; i++) {
+        const float* r = w + ((long)i * heads + a) * cols_full;
+        float* zr = z + (long)i * cols;
+        for (int j = 0; j < c8; j += 8) {
+            const __m256 s8 = _mm256_loadu_ps(sd + j);
+            const __m256 v = rh8(_mm256_div_ps(rh8(_mm256_sub_ps(_mm256_loadu_ps(r + j), _mm256_loadu_ps(mean + j))), s8));
+            _mm256_storeu_ps(zr + j, _mm256_blendv_ps(zero, v, _mm256_cmp_ps(s8, zero, _CMP_GT_OQ)));
+        }
+    }
+    if (c8 < cols) zscore_plain(w, rows, heads, a, cols_full, cols, z, mean, sd, c8);  // the last columns
+}
+
 // src/align.rs:6-63: w [rows][heads][cols_full]; one start time per row
 void jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out) {
     if (cols == 0) {
         std::fill(out, out + rows, 0.f);
         return;
     }
-    auto at = [&](int i, int a, int j) { return w[((long)i * heads + a) * cols_full + j]; };
     const int pad = width / 2;
+    static const bool avx2 = __builtin_cpu_supports("avx2") && __builtin_cpu_supports("f16c");
+    bool finite = true;
+    for (long i = 0; i < (long)rows * heads * cols_full && finite; i++) finite = std::isfinite(w[i]);
+    const bool fast = avx2 && finite;
     std::vector<float> avg((size_t)rows * cols, 0.f), z((size_t)rows * cols, 0.f);
-    std::vector<int32_t> win(width);
+    std::vector<float> mean(cols), sd(cols), acc(cols);
+    std::vector<int32_t> win(width), keys(cols), med(cols);
     for (int a = 0; a < heads; a++) {
-        for (int j = 0; j < cols; j++) {
-            float sum = -0.0f;  // Rust's f32 Sum starts from -0.0
-            for (int i = 0; i < rows; i++) sum += at(i, a, j);
-            const float mean_f = sum / (float)rows;
-            float vs = -0.0f;
-            for (int i = 0; i < rows; i++) {
-                const float t = at(i, a, j) - mean_f;
-                vs += t * t;
-            }
-            const float var = vs / (float)rows;
-            const float mean = rh(mean_f), sd = rh(std::sqrt(var));
-            // a constant column (always so for a single row) scores 0 (src/align.rs:22-23)
-            for (int i = 0; i < rows; i++) z[(long)i * cols + j] = sd > 0.f ? rh(rh(at(i, a, j) - mean) / sd) : 0.f;
-        }
+        if (fast) zscore_avx2(w, rows, heads, a, cols_full, cols, z.data(), mean.data(), sd.data(), acc.data());
+        else zscore_plain(w, rows, heads, a, cols_full, cols, z.data(), mean.data(), sd.data());
         for (int i = 0; i < rows; i++) {
             const float* row = &z[(long)i * cols];
             float* dst = &avg[(long)i * cols];
@@ -142,20 +229,30 @@ void jump_times(const float* w, int rows, int heads, int cols_full, int cols, in
                 for (int j = 0; j < cols; j++) dst[j] += row[j];
                 continue;
             }
+            // the median of the width-wide window with reflect padding, in f32::total_cmp order
+            for (int j = 0; j < cols; j++) keys[j] = total_key(row[j]);
+            int lo = cols, hi = cols;  // columns [lo, hi) take the branch-free interior path
+            if (width == 7 && cols > 6) {
+                lo = 3;
+                hi = cols - 3;
+                if (fast) median7_row_avx2(keys.data(), cols, med.data());
+                else median7_row_plain(keys.data(), cols, med.data());
+            }
             for (int j = 0; j < cols; j++) {
-                // median of the width-wide window with reflect padding, ordered by total_cmp
-                for (int k = 0; k < width; k++) {
-                    long t = (long)j + k - pad;
-                    if (t < 0) t = -t;
-                    else if (t >= cols) t = 2 * ((long)cols - 1) - t;
-                    win[k] = total_key(row[t]);
+                int32_t kmed;
+                if (j >= lo && j < hi) {
+                    kmed = med[j];
+                } else {
+                    for (int k = 0; k < width; k++) {
+                        long t = (long)j + k - pad;
+                        if (t < 0) t = -t;
+                        else if (t >= cols) t = 2 * ((long)cols - 1) - t;
+                        win[k] = keys[t];
+                    }
+                    std::nth_element(win.begin(), win.begin() + pad, win.end());
+                    kmed = win[pad];
                 }
-                std::nth_element(win.begin(), win.begin() + pad, win.end());
-                int32_t k = win[pad];
-                k ^= (int32_t)(((uint32_t)(k >> 31)) >> 1);  // the key map is its own inverse
-                float v;
-                std::memcpy(&v, &k, 4);
-                dst[j] += v;
+                dst[j] += key_to_f(kmed);
             }
         }
     }

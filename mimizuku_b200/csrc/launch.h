@@ -31,12 +31,14 @@ int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], con
 int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
                  const uint32_t box[3], bool swizzle128);
 
-void init_dec_attn_attrs();
+void init_dec_attn_attrs(DevCtx& c);
 void init_enc_attn_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
+size_t cross_attn_scratch_bytes(int batch, int d);
 int launch_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
-                      const int* done, int batch, int layer, int nl, int d, int na, int maxT, cudaStream_t st);
+                      const int* done, int batch, int layer, int nl, int d, int na, int maxT, void* scratch,
+                      size_t scratch_bytes, cudaStream_t st);
 int launch_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* ctr, const int* done, int batch,
                      int maxT, int d, cudaStream_t st);
 int launch_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch, int maxT, int d, cudaStream_t st);

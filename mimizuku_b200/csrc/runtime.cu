@@ -70,7 +70,7 @@ DevCtx& dev_ctx() {
     }
     c.status = (unsigned*)p;
     if (const char* s = getenv("MMZ_WAIT_LIMIT_MS")) c.limit_ns = (unsigned long long)atoll(s) * 1000000ull;
-    init_dec_attn_attrs();
+    init_dec_attn_attrs(c);
     init_enc_attn_attrs();
     cudaGetLastError();
     c.ok = true;

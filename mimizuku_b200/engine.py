@@ -137,3 +137,8 @@ class Engine:
     @property
     def allocated(self):
         return lib.mmz_engine_allocated(self._h)
+
+    @property
+    def launches(self):
+        """Kernels of the engine's kernel image launched so far (graph replays included, cuBLAS not)."""
+        return lib.mmz_engine_launches(self._h)
