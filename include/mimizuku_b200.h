@@ -71,6 +71,15 @@ int mmz_cross_attn(const void* q, const void* kv, void* out, void* align, const 
                    const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* scratch,
                    unsigned long long scratch_bytes, void* stream);
 unsigned long long mmz_cross_attn_scratch_bytes(int batch, int d);
+/* mmz_cross_attn for callers that cannot allocate device memory (a host that owns a fixed device-memory budget and
+ * forbids cudaMalloc after start-up, or a loop that cannot take cudaMalloc's implicit synchronisation): the same
+ * kernels and results, with the scratch in a static device array of the library (7.9 MB per device that loads the
+ * library, held until the process exits) instead of a caller buffer. It allocates nothing. Limit: batch x heads <= 640
+ * (32 sequences of a 20-head model); larger calls return an error. The first call on a device resolves the array's
+ * address and should come before any stream capture. Every call shares the array and clears its counters itself;
+ * calls that overlap on the GPU race on it and must be serialised by the caller. No counterpart in the reference. */
+int mmz_cross_attn_noalloc(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
+                           const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* stream);
 
 /* out = layernorm(x) per row of `dim` (even, <= 2048) fp16 values, fp32 statistics, eps as given.
  * Replaces layernorm (kernels/whisper.cu:66; src/model.rs:529-531). */

@@ -57,6 +57,7 @@ SIGNATURES = {
     "mmz_kv_write": (_I, [_P, _P, _P, _P, _I, _I, _I, _P]),
     "mmz_cross_attn": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _ULL, _P]),
     "mmz_cross_attn_scratch_bytes": (_ULL, [_I, _I]),
+    "mmz_cross_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     "mmz_layernorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _P]),
     "mmz_add_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _I, _F, _P]),
     "mmz_jump_times": (_I, [_FP, _I, _I, _I, _I, _I, _FP]),
@@ -176,6 +177,14 @@ def cross_attn(q, kv, out, align, aslot, ctr, done, layer, nl, d, na, max_t, scr
                          else cross_attn_scratch_bytes(b, d))
     _check(lib.mmz_cross_attn(_ptr(q), _ptr(kv), _ptr(out), _ptr(align), _ptr(aslot), _ptr(ctr), _ptr(done), b,
                               layer, nl, d, na, max_t, _ptr(scratch), scratch_bytes, _stream(stream)), "cross_attn")
+
+
+def cross_attn_noalloc(q, kv, out, align, aslot, ctr, done, layer, nl, d, na, max_t, batch=None, stream=None):
+    """cross_attn for callers that cannot allocate: the scratch is a static device array of the library (batch x
+    heads <= 640); calls that overlap on the GPU race on it."""
+    b = batch if batch is not None else done.shape[0]
+    _check(lib.mmz_cross_attn_noalloc(_ptr(q), _ptr(kv), _ptr(out), _ptr(align), _ptr(aslot), _ptr(ctr), _ptr(done),
+                                      b, layer, nl, d, na, max_t, _stream(stream)), "cross_attn_noalloc")
 
 
 def layernorm(x, w, b, out, eps=1e-5, rows=None, stream=None):

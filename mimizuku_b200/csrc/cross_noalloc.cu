@@ -1,0 +1,72 @@
+// mmz_cross_attn_noalloc: the decoder cross-attention of mmz_cross_attn for callers that cannot allocate device
+// memory. Some hosts hand a library no allocator and forbid cudaMalloc after start-up: a process embedded in an
+// application that owns a fixed device-memory budget, or a real-time loop that cannot take cudaMalloc's implicit
+// device synchronisation. Such a caller cannot provide the scratch buffer mmz_cross_attn asks for, so this entry point
+// brings its own: a file-scope device array of fixed size, which every GPU that loads the library holds until the
+// process exits.
+//
+// Limit: 640 (sequence, head) items per call, i.e. batch x heads <= 640 (32 sequences of Whisper large-v3, 20 heads),
+// 7.9 MB of scratch. Larger calls are rejected with an error.
+//
+// The array is shared by every call on a device and keeps the last call's contents. The per-item counters the
+// kernels need at zero are cleared by each call (with cudaMemsetAsync on the caller's stream, which allocates
+// nothing); calls that overlap on the GPU (other streams, other threads) race on the array and must be serialised
+// by the caller. The first call on a device resolves the array's device address (cudaGetSymbolAddress, with that
+// device current): make that first call before any stream capture.
+#include <mutex>
+
+#include "../../include/mimizuku_b200.h"
+#include "common.cuh"
+#include "launch.h"
+
+namespace mmz {
+
+constexpr int NOALLOC_MAX_ITEMS = 640;
+constexpr size_t NOALLOC_ITEM_BYTES = (size_t)TENC * 4 + 24 * 8 + 24 * HD * 4;  // S, stat and part of one item
+constexpr size_t NOALLOC_BYTES = NOALLOC_MAX_ITEMS * NOALLOC_ITEM_BYTES + ((NOALLOC_MAX_ITEMS * 4 + 255) / 256) * 256;
+
+static __device__ __align__(256) unsigned char g_cross_scratch[NOALLOC_BYTES];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64];  // device address of g_cross_scratch, per device
+
+// The array's device address on the current device, resolved once per device. In host code the symbol
+// g_cross_scratch is only a host-side stand-in; the kernels must be given this address.
+static int noalloc_scratch(void** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail("cross_attn_noalloc: no CUDA device");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_cross_scratch);
+        if (e != cudaSuccess || !p)
+            return failf("cross_attn_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return 0;
+}
+
+}  // namespace mmz
+
+using namespace mmz;
+
+extern "C" int mmz_cross_attn_noalloc(const void* q, const void* kv, void* out, void* align, const int* aslot,
+                                      const int* ctr, const int* done, int batch, int layer, int nl, int d, int na,
+                                      int max_t, void* stream) {
+    if (batch < 1 || d < HD || d % HD) return fail("cross_attn_noalloc: bad shape");
+    const long items = (long)batch * (d / HD);
+    const size_t need = cross_attn_scratch_bytes(batch, d);
+    if (items > NOALLOC_MAX_ITEMS || need > NOALLOC_BYTES)
+        return failf("cross_attn_noalloc: batch x heads = %ld exceeds the static scratch (%d items, %zu bytes); use "
+                     "mmz_cross_attn with a caller-provided scratch buffer",
+                     items, NOALLOC_MAX_ITEMS, NOALLOC_BYTES);
+    void* scratch = nullptr;
+    if (noalloc_scratch(&scratch)) return -1;
+    // the per-item counters (after S, stat and part) must start at zero
+    const size_t cnt_off = (size_t)items * NOALLOC_ITEM_BYTES;
+    const cudaError_t e = cudaMemsetAsync((char*)scratch + cnt_off, 0, (size_t)items * 4, (cudaStream_t)stream);
+    if (e != cudaSuccess) return failf("cross_attn_noalloc: clearing the counters failed: %s", cudaGetErrorString(e));
+    return launch_cross_attn(q, kv, out, align, aslot, ctr, done, batch, layer, nl, d, na, max_t, scratch, need,
+                             (cudaStream_t)stream);
+}
