@@ -256,6 +256,70 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 #undef MMZ_W8
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 32 TMEM lanes x 128 consecutive columns in one round trip (four loads, one wait)
+#define MMZ_R8(b) "=r"(r[b + 0]), "=r"(r[b + 1]), "=r"(r[b + 2]), "=r"(r[b + 3]), "=r"(r[b + 4]), "=r"(r[b + 5]), "=r"(r[b + 6]), "=r"(r[b + 7])
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%128];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,"
+        "%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%129];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,"
+        "%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%130];\n"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,"
+        "%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%131];\n"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : MMZ_R8(0), MMZ_R8(8), MMZ_R8(16), MMZ_R8(24), MMZ_R8(32), MMZ_R8(40), MMZ_R8(48), MMZ_R8(56), MMZ_R8(64),
+          MMZ_R8(72), MMZ_R8(80), MMZ_R8(88), MMZ_R8(96), MMZ_R8(104), MMZ_R8(112), MMZ_R8(120)
+        : "r"(taddr), "r"(taddr + 32), "r"(taddr + 64), "r"(taddr + 96)
+        : "memory");
+}
+#undef MMZ_R8
+
+// packed fp32 pairs (sm_100a): one instruction for two lanes of work
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+        " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
+        " mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for x <= 0 on the FMA pipe, two lanes at once: x = n + f with n = round(x) and f in [-0.5, 0.5];
+// 2^f by a degree-4 polynomial fitted (least squares at Chebyshev nodes, constant term fixed at 1) to 2^f on
+// [-0.5, 0.5], max relative error 5.4e-6; 2^n added into the exponent field. Inputs below -126 (the masked -inf
+// included) give 2^-126.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    const float magic = 12582912.0f;  // 1.5 * 2^23: adding it rounds to an integer held in the low mantissa bits
+    x.x = fmaxf(x.x, -126.f);
+    x.y = fmaxf(x.y, -126.f);
+    const float2 t = fadd2(x, make_float2(magic, magic));
+    const float2 n = fadd2(t, make_float2(-magic, -magic));
+    const float2 fr = ffma2(n, make_float2(-1.f, -1.f), x);
+    float2 p = make_float2(0.009550929069519043f, 0.009550929069519043f);
+    p = ffma2(p, fr, make_float2(0.055833350867033005f, 0.055833350867033005f));
+    p = ffma2(p, fr, make_float2(0.24024498462677002f, 0.24024498462677002f));
+    p = ffma2(p, fr, make_float2(0.6931373476982117f, 0.6931373476982117f));
+    p = ffma2(p, fr, make_float2(1.f, 1.f));
+    // bits(t) - bits(magic) = n; shifted into the exponent field the constant part of bits(magic) drops out
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -158,7 +158,9 @@ __global__ void __launch_bounds__(128)
 // ============================================================================ cross-attention kernels
 
 // Cross-attention as two streaming kernels with no waiting between CTAs: each CTA owns 192 positions of one
-// (sequence, head) and keeps all its 16-byte loads in flight at once (registers, no shared-memory staging).
+// (sequence, head); the scores kernel keeps all its 16-byte K loads in flight from registers, the P.V kernel pulls
+// its 24 KB V slice into shared memory with three bulk TMA copies (one per 64-position chunk) issued before it waits
+// for the scores.
 //   cross_scores_kernel  fp16-rounded scores and the three 64-position chunk statistics of its slice -> scratch
 //   cross_pv_kernel      issues its V loads, waits for the scores kernel (programmatic dependent launch), forms
 //                        the global maximum and sum from the 24 statistics in chunk order, the probabilities (and
@@ -167,20 +169,10 @@ __global__ void __launch_bounds__(128)
 // Scratch per launch: S [B][heads][1500] f32, stat [B][heads][24] float2, part [B][heads][24][64] f32, and one
 // counter per (sequence, head) that must start at zero and is left at zero.
 
-constexpr int XPOS_PER_THREAD = XPER / 16;  // positions a lane group of 8 handles: 12
-
 __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 
 struct XScratch {
     float* S;
@@ -207,22 +199,31 @@ __host__ __device__ inline XScratch cross_scratch(void* base, int batch, int nh)
     return x;
 }
 
-// grid (8, heads, B), block 128
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// grid (8, heads, B), block 128. Every thread's twelve 16-byte K loads are issued before any is used.
 __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict__ q, const h16* __restrict__ kv,
                                                            XScratch xs, const int* __restrict__ done, int layer,
                                                            int nl, int d) {
+    constexpr int PT = XPER / 16;  // positions per lane group of 8
     __shared__ float qs[HD];
     __shared__ float sc[XPER];
-    griddep_launch_dependents();  // the P.V kernel may start its V loads as soon as every CTA here is resident
+    griddep_launch_dependents();  // the P.V kernel may start its V copies as soon as every CTA here is resident
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
     const int nh = d / HD, bh = b * nh + hh;
     if (done[b]) return;
     const int j0 = r * XPER, n = min(XPER, TENC - j0);
     const int grp = t >> 3, sub = t & 7;
     const h16* K = kv + xkv_off(b, layer, 0, hh, nl, nh) + (long)j0 * HD + sub * 8;
-    uint4 u[XPOS_PER_THREAD];
+    uint4 u[PT];
 #pragma unroll
-    for (int i = 0; i < XPOS_PER_THREAD; i++) {
+    for (int i = 0; i < PT; i++) {
         const int jj = grp + 16 * i;
         u[i] = jj < n ? ldg_stream(K + jj * HD) : make_uint4(0, 0, 0, 0);
     }
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
     __syncthreads();
     // scores: a group of 8 lanes per position (kernels/whisper.cu:376-392)
 #pragma unroll
-    for (int i = 0; i < XPOS_PER_THREAD; i++) {
+    for (int i = 0; i < PT; i++) {
         const int jj = grp + 16 * i;
         const __half2* p2 = reinterpret_cast<const __half2*>(&u[i]);
         float a = 0.f;
@@ -263,23 +264,29 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
 __global__ void __launch_bounds__(128) cross_pv_kernel(const h16* __restrict__ kv, XScratch xs, h16* __restrict__ out,
                                                        h16* __restrict__ align, const int* __restrict__ aslot,
                                                        const int* __restrict__ ctr, const int* __restrict__ done,
-                                                       int layer, int nl, int d, int na, int maxT) {
+                                                       int layer, int nl, int d, int na, int maxT, unsigned* status,
+                                                       unsigned long long limit_ns) {
+    __shared__ __align__(128) h16 vs[XPER * HD];  // this CTA's V slice, bulk copies issued before the wait
     __shared__ float p[XPER];
     __shared__ float2 gs[XNCH];
     __shared__ float red[16][HD];
-    __shared__ int last;
+    __shared__ uint64_t bar[3];
+    __shared__ int last, abort;
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
     const int nh = d / HD, bh = b * nh + hh;
     if (done[b]) return;
     const int j0 = r * XPER, n = min(XPER, TENC - j0);
     const int grp = t >> 3, sub = t & 7;
-    // V does not depend on the scores: its loads are in flight before the wait
-    const h16* V = kv + xkv_off(b, layer, 1, hh, nl, nh) + (long)j0 * HD + sub * 8;
-    uint4 u[XPOS_PER_THREAD];
-#pragma unroll
-    for (int i = 0; i < XPOS_PER_THREAD; i++) {
-        const int jj = (i / 4) * XCH + grp + 16 * (i % 4);  // chunk i / 4, the group's positions in order
-        u[i] = jj < n ? ldg_stream(V + jj * HD) : make_uint4(0, 0, 0, 0);
+    if (t == 0) {  // V does not depend on the scores: its copies are in flight before the wait
+        abort = 0;
+        const h16* V = kv + xkv_off(b, layer, 1, hh, nl, nh) + (long)j0 * HD;
+        for (int c = 0; c < 3; c++) mbar_init(&bar[c], 1);
+        fence_mbar_init();
+        for (int c = 0; c < 3; c++) {
+            const int nc = min(XCH, n - c * XCH);
+            mbar_expect_tx(&bar[c], nc * HD * 2);
+            bulk_g2s(vs + c * XCH * HD, V + (long)c * XCH * HD, nc * HD * 2, &bar[c]);
+        }
     }
     griddep_wait();
     if (t < XNCH) gs[t] = __ldcg(&xs.stat[(long)bh * XNCH + t]);
@@ -303,19 +310,18 @@ __global__ void __launch_bounds__(128) cross_pv_kernel(const h16* __restrict__ k
     __syncthreads();
     // P.V per chunk: 16 groups x 8 lanes, a lane owns 8 of the 64 columns (kernels/whisper.cu:421-438)
     for (int c = 0; c < 3; c++) {
+        mbar_wait(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 4 + c);
+        const int nc = min(XCH, n - c * XCH);
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int jj = grp; jj < nc; jj += 16) {
+            const uint4 u = *reinterpret_cast<const uint4*>(vs + (c * XCH + jj) * HD + sub * 8);
+            const __half2* p2 = reinterpret_cast<const __half2*>(&u);
+            const float pj = p[c * XCH + jj];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int jj = c * XCH + grp + 16 * k;
-            if (jj < n) {
-                const __half2* p2 = reinterpret_cast<const __half2*>(&u[c * 4 + k]);
-                const float pj = p[jj];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    float2 v = __half22float2(p2[e]);
-                    a[2 * e] += pj * v.x;
-                    a[2 * e + 1] += pj * v.y;
-                }
+            for (int e = 0; e < 4; e++) {
+                float2 v = __half22float2(p2[e]);
+                a[2 * e] += pj * v.x;
+                a[2 * e + 1] += pj * v.y;
             }
         }
 #pragma unroll
@@ -342,6 +348,8 @@ __global__ void __launch_bounds__(128) cross_pv_kernel(const h16* __restrict__ k
         }
         if (t == 0) xs.cnt[bh] = 0;  // ready for the next launch
     }
+    if (t == 0 && abort)
+        for (int c = 0; c < 3; c++) mbar_wait(&bar[c], 0, nullptr, limit_ns, nullptr, 0, 0);
 }
 
 // kernels/whisper.cu:310-317 as its own launch (the engine folds it into self_attn_kernel): k and v of position p
@@ -385,7 +393,7 @@ int launch_cross_attn(const void* q, const void* kv, void* out, void* align, con
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, cross_pv_kernel, (const h16*)kv, xs, (h16*)out, (h16*)align, aslot, ctr,
-                                       done, layer, nl, d, na, maxT);
+                                       done, layer, nl, d, na, maxT, dc.status, dc.limit_ns);
     if (e != cudaSuccess) return failf("cross_pv: launch failed: %s", cudaGetErrorString(e));
     return 0;
 }

@@ -2,9 +2,9 @@
 // head size 64, fp16 in, fp32 accumulation (replaces enc_flash, kernels/whisper.cu:168-299 of the reference).
 //
 // One CTA computes a 128-query tile of one (clip, head) with the 5th-generation tensor cores:
-//   warp 0      TMA producer: Q once, then K and V tiles of 128 keys through a 2-stage ring (128-byte swizzle, read
+//   warp 0      TMA producers: Q once, then K and V tiles of 128 keys through 2-stage rings (128-byte swizzle, read
 //               straight out of the interleaved [clip][1500][3d] qkv buffer with a 3-D tensor map, which zero-fills
-//               the rows past 1500 of each clip)
+//               the rows past 1500 of each clip); a K stage is refilled as soon as its QK product is done
 //   warp 1      MMA issuer (one thread): S = Q K^T (M128 N128 K64) into TMEM, then O += P V (M128 N64 K128) with P
 //               from shared memory and V as an MN-major operand; completion is signalled with tcgen05.commit
 //   warps 2-5   softmax: thread i owns query row i of the tile (TMEM lane i), reads its 128 scores from TMEM,
@@ -43,7 +43,7 @@ struct Smem {
     uint8_t k[NSTAGE][TILE];
     uint8_t v[NSTAGE][TILE];
     uint8_t p[2][TILE];                      // P [128 rows][128 keys] as two K-major atoms of 64 keys
-    uint64_t bar_q, bar_kf[NSTAGE], bar_vf[NSTAGE], bar_kve[NSTAGE];
+    uint64_t bar_q, bar_kf[NSTAGE], bar_vf[NSTAGE], bar_ke[NSTAGE], bar_ve[NSTAGE];
     uint64_t bar_sf, bar_sfree, bar_pf, bar_od, bar_fin;
     uint32_t tmem;
     int abort;
@@ -81,7 +81,8 @@ __global__ void __launch_bounds__(192, 2)
         for (int i = 0; i < NSTAGE; i++) {
             mbar_init(&s.bar_kf[i], 1);
             mbar_init(&s.bar_vf[i], 1);
-            mbar_init(&s.bar_kve[i], 1);
+            mbar_init(&s.bar_ke[i], 1);
+            mbar_init(&s.bar_ve[i], 1);
         }
         mbar_init(&s.bar_sf, 1);
         mbar_init(&s.bar_sfree, 128);
@@ -101,27 +102,31 @@ __global__ void __launch_bounds__(192, 2)
     const uint32_t tS = tbase, tO = tbase + 128;
 
     if (warp == 0) {
-        // ---------------------------------------------------------------- TMA producer
-        if (lane == 0) {
-            prefetch_tmap(&qkv_map);
-            mbar_expect_tx(&s.bar_q, TILE);
-            tma_load_3d(s.q, &qkv_map, hh * HD, qt * BM, g, &s.bar_q);
+        // ---------------------------------------------------------------- TMA producers: lane 0 Q and K, lane 1 V
+        // (two queues, so a K tile is fetched as soon as its stage is free of the QK product that read it, without
+        // waiting behind V)
+        if (lane < 2) {
+            if (lane == 0) {
+                prefetch_tmap(&qkv_map);
+                mbar_expect_tx(&s.bar_q, TILE);
+                tma_load_3d(s.q, &qkv_map, hh * HD, qt * BM, g, &s.bar_q);
+            }
+            uint64_t* full = lane == 0 ? s.bar_kf : s.bar_vf;
+            uint64_t* empty = lane == 0 ? s.bar_ke : s.bar_ve;
+            uint8_t(*dst)[TILE] = lane == 0 ? s.k : s.v;
+            const int col = (lane == 0 ? d : 2 * d) + hh * HD;
             int issued = 0;
             for (int j = 0; j < NKT; j++) {
                 const int st = j % NSTAGE, n = j / NSTAGE;
-                if (n > 0 && !mbar_wait(&s.bar_kve[st], (n - 1) & 1, abort, limit_ns, status, K_ENC, 10)) break;
-                mbar_expect_tx(&s.bar_kf[st], TILE);
-                tma_load_3d(s.k[st], &qkv_map, d + hh * HD, j * BN, g, &s.bar_kf[st]);
-                mbar_expect_tx(&s.bar_vf[st], TILE);
-                tma_load_3d(s.v[st], &qkv_map, 2 * d + hh * HD, j * BN, g, &s.bar_vf[st]);
+                if (n > 0 && !mbar_wait(&empty[st], (n - 1) & 1, abort, limit_ns, status, K_ENC, 10 + lane)) break;
+                mbar_expect_tx(&full[st], TILE);
+                tma_load_3d(dst[st], &qkv_map, col, j * BN, g, &full[st]);
                 issued = j + 1;
             }
             if (*abort) {  // let every issued copy land before the shared memory is released
-                mbar_wait(&s.bar_q, 0, nullptr, limit_ns, nullptr, 0, 0);
-                for (int j = issued > NSTAGE ? issued - NSTAGE : 0; j < issued; j++) {
-                    mbar_wait(&s.bar_kf[j % NSTAGE], (j / NSTAGE) & 1, nullptr, limit_ns, nullptr, 0, 0);
-                    mbar_wait(&s.bar_vf[j % NSTAGE], (j / NSTAGE) & 1, nullptr, limit_ns, nullptr, 0, 0);
-                }
+                if (lane == 0) mbar_wait(&s.bar_q, 0, nullptr, limit_ns, nullptr, 0, 0);
+                for (int j = issued > NSTAGE ? issued - NSTAGE : 0; j < issued; j++)
+                    mbar_wait(&full[j % NSTAGE], (j / NSTAGE) & 1, nullptr, limit_ns, nullptr, 0, 0);
             }
         }
     } else if (warp == 1) {
@@ -138,6 +143,7 @@ __global__ void __launch_bounds__(192, 2)
                     umma_f16_ss(tS, sdesc_sw128(qa + kk * 32, 16, SBO), sdesc_sw128(ka + kk * 32, 16, SBO), IDESC_QK,
                                 kk > 0);
                 umma_commit(&s.bar_sf);
+                umma_commit(&s.bar_ke[0]);
             }
             for (int j = 0; ok && j < NKT; j++) {
                 const int st = j % NSTAGE;
@@ -153,6 +159,7 @@ __global__ void __launch_bounds__(192, 2)
                         umma_f16_ss(tS, sdesc_sw128(qa + kk * 32, 16, SBO), sdesc_sw128(ka + kk * 32, 16, SBO),
                                     IDESC_QK, kk > 0);
                     umma_commit(&s.bar_sf);
+                    umma_commit(&s.bar_ke[st1]);
                 }
                 ok = mbar_wait(&s.bar_pf, j & 1, abort, limit_ns, status, K_ENC, 24) &&
                      mbar_wait(&s.bar_vf[st], (j / NSTAGE) & 1, abort, limit_ns, status, K_ENC, 25);
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(192, 2)
                                 (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&s.bar_od);
-                umma_commit(&s.bar_kve[st]);
+                umma_commit(&s.bar_ve[st]);
             }
             umma_commit(&s.bar_fin);  // completes once every MMA issued above has finished
         }
@@ -183,58 +190,71 @@ __global__ void __launch_bounds__(192, 2)
             ok = __all_sync(0xffffffff, mbar_wait(&s.bar_sf, j & 1, abort, limit_ns, status, K_ENC, 30));
             if (!ok) break;
             tc_fence_after();
-            float sv[BN];
-#pragma unroll
-            for (int c4 = 0; c4 < BN / 32; c4++) {
-                uint32_t r[32];
-                tmem_ld32(tS + loff + c4 * 32, r);
-#pragma unroll
-                for (int i = 0; i < 32; i++) sv[c4 * 32 + i] = __uint_as_float(r[i]);
-            }
+            uint32_t raw[BN];
+            tmem_ld128(tS + loff, raw);
             tc_fence_before();
             mbar_arrive(&s.bar_sfree);
+            float* sv = reinterpret_cast<float*>(raw);
             if (j == NKT - 1) {  // keys past 1500 (zero-filled by the copy) take no weight
 #pragma unroll
                 for (int c = LAST_VALID; c < BN; c++) sv[c] = -INFINITY;
             }
-            float tmax = -INFINITY;
+            float tmax = fmaxf(sv[0], sv[1]);
 #pragma unroll
-            for (int c = 0; c < BN; c++) tmax = fmaxf(tmax, sv[c]);
+            for (int c = 2; c < BN; c += 2) tmax = fmax3(tmax, sv[c], sv[c + 1]);
             const float mn = fmaxf(m, tmax * sl2);
             const float corr = ex2_approx(m - mn);
             m = mn;
-            uint32_t pk[BN / 2];
-            float rs = 0.f;
+            // exponentials of one pair of columns: a quarter of them on the FMA pipe (exp2_poly2), the rest on MUFU
+            const float2 sl2_2 = make_float2(sl2, sl2), nmn2 = make_float2(-mn, -mn);
+            float2 rs2 = make_float2(0.f, 0.f);
+            auto pexp = [&](int c) -> uint32_t {
+                const float2 x = ffma2(make_float2(sv[2 * c], sv[2 * c + 1]), sl2_2, nmn2);
+                float2 e;
+                if ((c & 3) == 3) {
+                    e = exp2_poly2(x);
+                } else {
+                    e.x = ex2_approx(x.x);
+                    e.y = ex2_approx(x.y);
+                }
+                rs2 = fadd2(rs2, e);
+                return pack_h2(e.x, e.y);
+            };
+            // P row into the 128-byte swizzled K-major tile: 16-byte chunk c of a 128-byte row lands at c ^ (row % 8)
+            auto pstore = [&](int c16, uint32_t a, uint32_t b, uint32_t c, uint32_t d4) {
+                const uint32_t addr = pbase + (c16 >> 3) * TILE + row * 128 + (((c16 & 7) ^ (row & 7)) << 4);
+                st_shared_v4(addr, a, b, c, d4);
+            };
+            // the first half of P is held in registers while the previous P.V may still read the P buffer
+            uint32_t pk[BN / 4];
 #pragma unroll
-            for (int c = 0; c < BN / 2; c++) {
-                const float p0 = ex2_approx(fmaf(sv[2 * c], sl2, -mn));
-                const float p1 = ex2_approx(fmaf(sv[2 * c + 1], sl2, -mn));
-                rs += p0 + p1;
-                pk[c] = pack_h2(p0, p1);
-            }
-            l = l * corr + rs;
+            for (int c = 0; c < BN / 4; c++) pk[c] = pexp(c);
             if (j > 0) {
                 // P.V of the previous tile must be complete: it reads the P buffer and accumulates into O
                 ok = __all_sync(0xffffffff, mbar_wait(&s.bar_od, (j - 1) & 1, abort, limit_ns, status, K_ENC, 31));
                 if (!ok) break;
                 tc_fence_after();
-                if (__any_sync(0xffffffff, corr != 1.f)) {
-#pragma unroll
-                    for (int c2 = 0; c2 < HD / 32; c2++) {
-                        uint32_t r[32];
-                        tmem_ld32(tO + loff + c2 * 32, r);
-#pragma unroll
-                        for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-                        tmem_st32(tO + loff + c2 * 32, r);
-                    }
-                    tmem_wait_st();
-                }
             }
-            // P row into the 128-byte swizzled K-major tile: 16-byte chunk c of a 128-byte row lands at c ^ (row % 8)
 #pragma unroll
-            for (int c16 = 0; c16 < BN / 8; c16++) {
-                const uint32_t addr = pbase + (c16 >> 3) * TILE + row * 128 + (((c16 & 7) ^ (row & 7)) << 4);
-                st_shared_v4(addr, pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+            for (int c16 = 0; c16 < BN / 16; c16++) pstore(c16, pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+            // the second half streams straight into the tile
+#pragma unroll
+            for (int c16 = BN / 16; c16 < BN / 8; c16++) {
+                const uint32_t a = pexp(4 * c16), b = pexp(4 * c16 + 1), c = pexp(4 * c16 + 2), d4 = pexp(4 * c16 + 3);
+                pstore(c16, a, b, c, d4);
+            }
+            l = l * corr + (rs2.x + rs2.y);
+            // the running max moved: rescale this row of O before the next P.V accumulates into it
+            if (j > 0 && __any_sync(0xffffffff, corr != 1.f)) {
+#pragma unroll
+                for (int c2 = 0; c2 < HD / 32; c2++) {
+                    uint32_t r[32];
+                    tmem_ld32(tO + loff + c2 * 32, r);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+                    tmem_st32(tO + loff + c2 * 32, r);
+                }
+                tmem_wait_st();
             }
             fence_proxy_async_smem();
             tc_fence_before();
