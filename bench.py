@@ -312,9 +312,11 @@ def main():
     d2h = 4 * CLIPS_PER_GPU * cfg.max_t + 2 * CLIPS_PER_GPU * (NEW_TOKENS - 1) * e.na * 1500
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
-            traffic = json.load(f).get("cross_attn_bytes_per_launch")
-    except Exception:
+        with open(os.path.join(ROOT, "profiles", "cross_attn_traffic.txt")) as f:
+            for ln in f:
+                if ln.startswith("cross_attn_bytes_per_launch"):
+                    traffic = int(ln.split()[1])
+    except OSError:
         pass
     line = {
         "metric": METRIC,

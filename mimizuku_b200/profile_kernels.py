@@ -1,0 +1,58 @@
+"""Runs one hot kernel four times at the benchmark's shapes, for an ncu capture of a single launch
+(e.g. ncu --set full --clock-control none -k regex:enc_flash -s 2 -c 1 ...):
+
+    python -m mimizuku_b200.profile_kernels enc            encoder attention, large-v3, 8 clips x 20 heads
+    python -m mimizuku_b200.profile_kernels cross          cross-attention, large-v3, batch 32, one layer
+    python -m mimizuku_b200.profile_kernels self [p]       self-attention, large-v3, batch 32, position p (default 223)
+"""
+import sys
+
+import torch
+
+import mimizuku_b200 as m
+
+
+def main(argv):
+    which = argv[0] if argv else "enc"
+    m.init(0)
+    torch.manual_seed(0)
+    if which == "enc":
+        g, d = 8, 1280
+        qkv = torch.randn(g, 1500, 3 * d, device="cuda", dtype=torch.float16)
+        out = torch.empty(g, 1500, d, device="cuda", dtype=torch.float16)
+        for _ in range(4):
+            m.enc_flash(qkv, out, d)
+    elif which == "cross":
+        B, d, nl, nh, mt, na = 32, 1280, 1, 20, 448, 10
+        kv = torch.randn(B, nl, 2, nh, 1500, 64, device="cuda", dtype=torch.float16)
+        q = torch.randn(B, d, device="cuda", dtype=torch.float16)
+        aslot = torch.full((nl * nh,), -1, dtype=torch.int32, device="cuda")
+        aslot[:na] = torch.arange(na, dtype=torch.int32, device="cuda")
+        align = torch.zeros(B, mt, na, 1500, dtype=torch.float16, device="cuda")
+        ctr = torch.tensor([100, 0, 0, 0], dtype=torch.int32, device="cuda")
+        done = torch.zeros(B, dtype=torch.int32, device="cuda")
+        out = torch.zeros(B, d, dtype=torch.float16, device="cuda")
+        scratch = torch.zeros(m.cross_attn_scratch_bytes(B, d), dtype=torch.uint8, device="cuda")
+        for _ in range(4):
+            m.cross_attn(q, kv, out, align, aslot, ctr, done, 0, nl, d, na, mt, scratch)
+    elif which == "self":
+        B, d, mt = 32, 1280, 448
+        p = int(argv[1]) if len(argv) > 1 else 223
+        kc = torch.randn(B, mt, d, device="cuda", dtype=torch.float16)
+        vc = torch.randn(B, mt, d, device="cuda", dtype=torch.float16)
+        qkv = torch.randn(B, 3 * d, device="cuda", dtype=torch.float16)
+        done = torch.zeros(B, dtype=torch.int32, device="cuda")
+        out = torch.zeros(B, d, dtype=torch.float16, device="cuda")
+        ctr = torch.tensor([p, 0, 0, 0], dtype=torch.int32, device="cuda")
+        for _ in range(4):
+            m.self_attn(qkv, kc, vc, out, ctr, done, mt, d)
+    else:
+        raise SystemExit(__doc__)
+    torch.cuda.synchronize()
+    if m.status()[0] != 0:
+        raise SystemExit(f"kernel status word {m.status()}")
+    print("ok", which)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
