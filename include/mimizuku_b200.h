@@ -61,12 +61,12 @@ int mmz_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch,
  * head-contiguous cross k/v buffer [batch][nl][k|v][heads][1500][64], out [batch][d]. For the heads with
  * aslot[layer * heads + head] = s >= 0, the fp16 probabilities are also stored into align[b][ctr[0]][s][1500]
  * (align is [batch][max_t][na][1500]). Sequences with done[b] != 0 are skipped.
- * Two streaming split-KV kernels (scores and 64-position chunk statistics; then probabilities, P.V and the in-order
- * combine of the 24 chunk partials by the last CTA of each (sequence, head)), the second a programmatic dependent
- * launch of the first. Replaces cross_scores + cross_pv + cross_combine (kernels/whisper.cu:368, :407, :443;
+ * Three kernels chained by programmatic dependent launches: split-KV scores and 64-position chunk statistics; then
+ * probabilities and per-chunk P.V partials; then the in-order combine of the 24 chunk partials of each
+ * (sequence, head). Replaces cross_scores + cross_pv + cross_combine (kernels/whisper.cu:368, :407, :443;
  * src/model.rs:676-705), whose S / stat / part buffers (model.rs:452-454) become `scratch`: a device buffer of at
- * least mmz_cross_attn_scratch_bytes(batch, d) bytes, 16-byte aligned and zeroed once before its first use (the kernels
- * leave it reusable). Launches that share a scratch buffer must not overlap on the GPU. kv 16-byte aligned. */
+ * least mmz_cross_attn_scratch_bytes(batch, d) bytes, 16-byte aligned, with no initial contents required.
+ * Launches that share a scratch buffer must not overlap on the GPU. kv 16-byte aligned. */
 int mmz_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
                    const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* scratch,
                    unsigned long long scratch_bytes, void* stream);
@@ -76,8 +76,8 @@ unsigned long long mmz_cross_attn_scratch_bytes(int batch, int d);
  * kernels and results, with the scratch in a static device array of the library (7.9 MB per device that loads the
  * library, held until the process exits) instead of a caller buffer. It allocates nothing. Limit: batch x heads <= 640
  * (32 sequences of a 20-head model); larger calls return an error. The first call on a device resolves the array's
- * address and should come before any stream capture. Every call shares the array and clears its counters itself;
- * calls that overlap on the GPU race on it and must be serialised by the caller. No counterpart in the reference. */
+ * address and should come before any stream capture. Every call shares the array; calls that overlap on the GPU
+ * race on it and must be serialised by the caller. No counterpart in the reference. */
 int mmz_cross_attn_noalloc(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
                            const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* stream);
 

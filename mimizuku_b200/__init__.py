@@ -169,8 +169,8 @@ def cross_attn_scratch_bytes(batch, d):
 
 def cross_attn(q, kv, out, align, aslot, ctr, done, layer, nl, d, na, max_t, scratch, batch=None, stream=None,
                scratch_bytes=None):
-    """kernels/whisper.cu:368-449 cross_scores + cross_pv + cross_combine as two streaming kernels. scratch: a
-    zeroed device buffer (torch tensor or address) of at least cross_attn_scratch_bytes(batch, d) bytes."""
+    """kernels/whisper.cu:368-449 cross_scores + cross_pv + cross_combine as three chained kernels. scratch: a device
+    buffer (torch tensor or address) of at least cross_attn_scratch_bytes(batch, d) bytes."""
     b = batch if batch is not None else done.shape[0]
     if scratch_bytes is None:
         scratch_bytes = (scratch.numel() * scratch.element_size() if hasattr(scratch, "numel")

@@ -8,10 +8,9 @@
 // Limit: 640 (sequence, head) items per call, i.e. batch x heads <= 640 (32 sequences of Whisper large-v3, 20 heads),
 // 7.9 MB of scratch. Larger calls are rejected with an error.
 //
-// The array is shared by every call on a device and keeps the last call's contents. The per-item counters the
-// kernels need at zero are cleared by each call (with cudaMemsetAsync on the caller's stream, which allocates
-// nothing); calls that overlap on the GPU (other streams, other threads) race on the array and must be serialised
-// by the caller. The first call on a device resolves the array's device address (cudaGetSymbolAddress, with that
+// The array is shared by every call on a device and keeps the last call's contents; nothing in it needs to start at
+// zero (every value a call reads was written earlier in the same call). Calls that overlap on the GPU (other streams,
+// other threads) race on the array and must be serialised by the caller. The first call on a device resolves the array's device address (cudaGetSymbolAddress, with that
 // device current): make that first call before any stream capture.
 #include <mutex>
 
@@ -23,7 +22,7 @@ namespace mmz {
 
 constexpr int NOALLOC_MAX_ITEMS = 640;
 constexpr size_t NOALLOC_ITEM_BYTES = (size_t)TENC * 4 + 24 * 8 + 24 * HD * 4;  // S, stat and part of one item
-constexpr size_t NOALLOC_BYTES = NOALLOC_MAX_ITEMS * NOALLOC_ITEM_BYTES + ((NOALLOC_MAX_ITEMS * 4 + 255) / 256) * 256;
+constexpr size_t NOALLOC_BYTES = NOALLOC_MAX_ITEMS * NOALLOC_ITEM_BYTES;
 
 static __device__ __align__(256) unsigned char g_cross_scratch[NOALLOC_BYTES];
 
@@ -63,10 +62,6 @@ extern "C" int mmz_cross_attn_noalloc(const void* q, const void* kv, void* out, 
                      items, NOALLOC_MAX_ITEMS, NOALLOC_BYTES);
     void* scratch = nullptr;
     if (noalloc_scratch(&scratch)) return -1;
-    // the per-item counters (after S, stat and part) must start at zero
-    const size_t cnt_off = (size_t)items * NOALLOC_ITEM_BYTES;
-    const cudaError_t e = cudaMemsetAsync((char*)scratch + cnt_off, 0, (size_t)items * 4, (cudaStream_t)stream);
-    if (e != cudaSuccess) return failf("cross_attn_noalloc: clearing the counters failed: %s", cudaGetErrorString(e));
     return launch_cross_attn(q, kv, out, align, aslot, ctr, done, batch, layer, nl, d, na, max_t, scratch, need,
                              (cudaStream_t)stream);
 }

@@ -4,7 +4,8 @@
 //   self-attention   one CTA per (sequence, head) streams its K then V rows through an 8-deep ring of TMA tensor
 //                    copies; the reference's thread mapping makes every sum run in the reference's order
 //   cross-attention  split-KV over 8 slices of 192 positions per (sequence, head), as two streaming kernels with
-//                    every 16-byte load of a thread in flight at once, joined by a programmatic dependent launch
+//                    every 16-byte load of a thread in flight at once and a small combine, chained by programmatic
+//                    dependent launches
 //
 // Both read the position from device memory (ctr[0]) and skip finished sequences (done[b]), so one captured CUDA graph
 // serves every decoding step, as the reference engine requires (kernels/whisper.cu:7-8).
@@ -157,17 +158,16 @@ __global__ void __launch_bounds__(128)
 
 // ============================================================================ cross-attention kernels
 
-// Cross-attention as two streaming kernels with no waiting between CTAs: each CTA owns 192 positions of one
+// Cross-attention as three kernels with no waiting between CTAs: each CTA of the first two owns 192 positions of one
 // (sequence, head); the scores kernel keeps all its 16-byte K loads in flight from registers, the P.V kernel pulls
 // its 24 KB V slice into shared memory with three bulk TMA copies (one per 64-position chunk) issued before it waits
 // for the scores.
-//   cross_scores_kernel  fp16-rounded scores and the three 64-position chunk statistics of its slice -> scratch
-//   cross_pv_kernel      issues its V loads, waits for the scores kernel (programmatic dependent launch), forms
-//                        the global maximum and sum from the 24 statistics in chunk order, the probabilities (and
-//                        the alignment rows), its three per-chunk P.V partials -> scratch; the last CTA of the
-//                        (sequence, head) to finish sums the 24 partials in chunk order.
-// Scratch per launch: S [B][heads][1500] f32, stat [B][heads][24] float2, part [B][heads][24][64] f32, and one
-// counter per (sequence, head) that must start at zero and is left at zero.
+//   cross_scores_kernel   fp16-rounded scores and the three 64-position chunk statistics of its slice -> scratch
+//   cross_pv_kernel       issues its V loads, waits for the scores kernel (programmatic dependent launch), forms
+//                         the global maximum and sum from the 24 statistics in chunk order, the probabilities (and
+//                         the alignment rows), its three per-chunk P.V partials -> scratch
+//   cross_combine_kernel  waits for the P.V kernel the same way and sums the 24 partials in chunk order
+// Scratch per launch: S [B][heads][1500] f32, stat [B][heads][24] float2, part [B][heads][24][64] f32.
 
 __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -178,12 +178,11 @@ struct XScratch {
     float* S;
     float2* stat;
     float* part;
-    int* cnt;
 };
 
 __host__ __device__ inline size_t cross_scratch_bytes(int batch, int nh) {
     const size_t items = (size_t)batch * nh;
-    return items * TENC * 4 + items * XNCH * 8 + items * XNCH * HD * 4 + ((items * 4 + 255) / 256) * 256;
+    return items * TENC * 4 + items * XNCH * 8 + items * XNCH * HD * 4;
 }
 __host__ __device__ inline XScratch cross_scratch(void* base, int batch, int nh) {
     const size_t items = (size_t)batch * nh;
@@ -194,8 +193,6 @@ __host__ __device__ inline XScratch cross_scratch(void* base, int batch, int nh)
     x.stat = (float2*)p;
     p += items * XNCH * 8;
     x.part = (float*)p;
-    p += items * XNCH * HD * 4;
-    x.cnt = (int*)p;
     return x;
 }
 
@@ -261,17 +258,18 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
 }
 
 // grid (8, heads, B), block 128; launched as a programmatic dependent of cross_scores_kernel
-__global__ void __launch_bounds__(128) cross_pv_kernel(const h16* __restrict__ kv, XScratch xs, h16* __restrict__ out,
-                                                       h16* __restrict__ align, const int* __restrict__ aslot,
-                                                       const int* __restrict__ ctr, const int* __restrict__ done,
-                                                       int layer, int nl, int d, int na, int maxT, unsigned* status,
-                                                       unsigned long long limit_ns) {
+__global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict__ kv, XScratch xs,
+                                                          h16* __restrict__ align, const int* __restrict__ aslot,
+                                                          const int* __restrict__ ctr, const int* __restrict__ done,
+                                                          int layer, int nl, int d, int na, int maxT, unsigned* status,
+                                                          unsigned long long limit_ns) {
     __shared__ __align__(128) h16 vs[XPER * HD];  // this CTA's V slice, bulk copies issued before the wait
     __shared__ float p[XPER];
     __shared__ float2 gs[XNCH];
-    __shared__ float red[16][HD];
+    __shared__ float red[3][16][HD];
     __shared__ uint64_t bar[3];
-    __shared__ int last, abort;
+    __shared__ int abort;
+    griddep_launch_dependents();  // the combine kernel may be scheduled as soon as every CTA here is resident
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
     const int nh = d / HD, bh = b * nh + hh;
     if (done[b]) return;
@@ -308,7 +306,8 @@ __global__ void __launch_bounds__(128) cross_pv_kernel(const h16* __restrict__ k
         if (arow) arow[jj] = h(pj);
     }
     __syncthreads();
-    // P.V per chunk: 16 groups x 8 lanes, a lane owns 8 of the 64 columns (kernels/whisper.cu:421-438)
+    // P.V per chunk: 16 groups x 8 lanes, a lane owns 8 of the 64 columns (kernels/whisper.cu:421-438); the three
+    // chunks' group sums meet in shared memory behind one barrier
     for (int c = 0; c < 3; c++) {
         mbar_wait(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 4 + c);
         const int nc = min(XCH, n - c * XCH);
@@ -325,31 +324,30 @@ __global__ void __launch_bounds__(128) cross_pv_kernel(const h16* __restrict__ k
             }
         }
 #pragma unroll
-        for (int e = 0; e < 8; e++) red[grp][sub * 8 + e] = a[e];
-        __syncthreads();
-        if (t < HD) {
-            float acc = 0.f;
-            for (int g = 0; g < 16; g++) acc += red[g][t];
-            xs.part[((long)bh * XNCH + r * 3 + c) * HD + t] = acc;
-        }
-        __syncthreads();
+        for (int e = 0; e < 8; e++) red[c][grp][sub * 8 + e] = a[e];
     }
-    // the last of the 8 CTAs of this (sequence, head) sums the 24 partials in order (kernels/whisper.cu:443-449)
-    __threadfence();
     __syncthreads();
-    if (t == 0) last = atomicAdd(&xs.cnt[bh], 1) == XCL - 1;
-    __syncthreads();
-    if (last) {
-        __threadfence();
-        if (t < HD) {
-            float acc = 0.f;
-            for (int c = 0; c < XNCH; c++) acc += __ldcg(&xs.part[((long)bh * XNCH + c) * HD + t]);
-            out[(long)b * d + hh * HD + t] = h(acc);
-        }
-        if (t == 0) xs.cnt[bh] = 0;  // ready for the next launch
+    for (int i = t; i < 3 * HD; i += 128) {
+        const int c = i / HD, col = i % HD;
+        float acc = 0.f;
+        for (int g = 0; g < 16; g++) acc += red[c][g][col];
+        xs.part[((long)bh * XNCH + r * 3 + c) * HD + col] = acc;
     }
     if (t == 0 && abort)
         for (int c = 0; c < 3; c++) mbar_wait(&bar[c], 0, nullptr, limit_ns, nullptr, 0, 0);
+}
+
+// grid (heads, B), block 64; launched as a programmatic dependent of cross_pv_kernel: the 24 partials of a
+// (sequence, head) summed in chunk order (kernels/whisper.cu:443-449)
+__global__ void __launch_bounds__(64) cross_combine_kernel(const float* __restrict__ part, h16* __restrict__ out,
+                                                           const int* __restrict__ done, int d) {
+    const int hh = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+    const int bh = b * (d / HD) + hh;
+    griddep_wait();
+    if (done[b]) return;
+    float acc = 0.f;
+    for (int c = 0; c < XNCH; c++) acc += __ldcg(&part[((long)bh * XNCH + c) * HD + t]);
+    out[(long)b * d + hh * HD + t] = h(acc);
 }
 
 // kernels/whisper.cu:310-317 as its own launch (the engine folds it into self_attn_kernel): k and v of position p
@@ -392,9 +390,13 @@ int launch_cross_attn(const void* q, const void* kv, void* out, void* align, con
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, cross_pv_kernel, (const h16*)kv, xs, (h16*)out, (h16*)align, aslot, ctr,
-                                       done, layer, nl, d, na, maxT, dc.status, dc.limit_ns);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, cross_pv_kernel, (const h16*)kv, xs, (h16*)align, aslot, ctr, done,
+                                       layer, nl, d, na, maxT, dc.status, dc.limit_ns);
     if (e != cudaSuccess) return failf("cross_pv: launch failed: %s", cudaGetErrorString(e));
+    cfg.gridDim = dim3(d / HD, batch, 1);
+    cfg.blockDim = dim3(HD, 1, 1);
+    e = cudaLaunchKernelEx(&cfg, cross_combine_kernel, (const float*)xs.part, (h16*)out, done, d);
+    if (e != cudaSuccess) return failf("cross_combine: launch failed: %s", cudaGetErrorString(e));
     return 0;
 }
 

@@ -74,11 +74,11 @@ class NativeKernels : public Kernels {
                   int d, int, cudaStream_t st) override {
         return ++launches, launch_self_attn(qkv, kc, vc, att, ctr, done, b, maxT, d, st);
     }
-    // two streaming kernels joined by a programmatic dependent launch, on the engine's cross-attention scratch
+    // three kernels chained by programmatic dependent launches, on the engine's cross-attention scratch
     int cross_attn(const void* xq, const void* kv, void*, void*, void*, void* att, void* align, const int* aslot,
                    const int* ctr, const int* done, int b, int layer, int nl, int d, int, int na, int maxT,
                    cudaStream_t st) override {
-        launches += 2;
+        launches += 3;
         return launch_cross_attn(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, xscratch,
                                  xscratch_bytes, st);
     }
@@ -385,7 +385,7 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         s_ = alloc(b * nh * TENC_ * 4);
         stat_ = alloc(b * nh * NCH * 8);
         part_ = alloc(b * nh * NCH * HDIM * 4);
-    } else {  // the native kernels' scratch for the same role (zero-filled, as the kernels require)
+    } else {  // the native kernels' scratch for the same role
         NativeKernels* nk = static_cast<NativeKernels*>(k_.get());
         nk->xscratch_bytes = cross_attn_scratch_bytes(bmax, d);
         nk->xscratch = alloc(nk->xscratch_bytes);

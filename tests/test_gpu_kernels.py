@@ -111,7 +111,7 @@ def test_cross_attn(cuda, ref, B, d, nl, layer, p):
     ALNr = torch.zeros_like(ALN)
     OUT = torch.zeros(B, d, dtype=torch.float16, device="cuda")
     scratch = torch.zeros(m.cross_attn_scratch_bytes(B, d), dtype=torch.uint8, device="cuda")
-    for _ in range(2):  # twice: the scratch (its per-item counters) must be left reusable
+    for _ in range(2):  # twice: the scratch must be reusable without clearing
         m.cross_attn(Q, KV, OUT, ALN, ASL, CTR, DONE, layer, nl, d, na, max_t, scratch)
     OUTr = _ref_cross(ref, torch, Q, KV, ALNr, ASL, CTR, DONE, B, layer, nl, d, na, max_t)
     torch.cuda.synchronize()
