@@ -248,12 +248,20 @@ def main():
     steps_dec = np_ - 1 + NEW_TOKENS
     st = torch.cuda.ExternalStream(e.stream)
 
+    if args.impl == "native":  # the timestamp cost is reduced on the GPU (the reference does it on the host)
+        rc_dev = torch.tensor([NEW_TOKENS - 1] * CLIPS_PER_GPU + [int(f) // 2 for f in frames], dtype=torch.int32,
+                              device="cuda")
+        cost_dev = torch.empty((CLIPS_PER_GPU, cfg.max_t, 1500), dtype=torch.float32, device="cuda")
+
     def gpu_pipeline():
         for g0 in range(0, CLIPS_PER_GPU, 8):
             e.encode(mel16[g0].data_ptr(), 8, g0)
         e.reset(np.tile(prompt, (CLIPS_PER_GPU, 1)))
         for _ in range(steps_dec):
             e.replay()
+        if args.impl == "native":
+            m.align_cost(e.buffer("align"), rc_dev[:CLIPS_PER_GPU], rc_dev[CLIPS_PER_GPU:], np_, cfg.max_t, e.na,
+                         cost_dev, n=CLIPS_PER_GPU, stream=e.stream)
 
     def barrier():
         if dist:
@@ -282,7 +290,7 @@ def main():
             gpu_pipeline()
         b.record(st)
         b.synchronize()
-    launches = e.launches - launches0
+    launches = e.launches - launches0 + (args.steps if args.impl == "native" else 0)  # + the cost kernels
     t_dev = max_over_ranks(a.elapsed_time(b) * 1e-3)
     torch.cuda.synchronize()
     barrier()
@@ -309,7 +317,7 @@ def main():
     value = n_total * args.steps / t_dev
     e2e = n_total * args.steps / t_e2e
     h2d = mel.nbytes + 4 * CLIPS_PER_GPU * np_
-    d2h = 4 * CLIPS_PER_GPU * cfg.max_t + 2 * CLIPS_PER_GPU * (NEW_TOKENS - 1) * e.na * 1500
+    d2h = e.d2h_bytes  # tokens, and the recorded probabilities (reference) or the DTW cost rows (native)
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "cross_attn_traffic.txt")) as f:

@@ -94,6 +94,16 @@ int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void
 /* w [rows][heads][cols_full] alignment-head probabilities -> out [rows] start times in seconds (cols = audio frames
  * / 2, width = median filter width, 7 in the reference). src/align.rs:8-63. */
 int mmz_jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out);
+/* The two halves of mmz_jump_times, the first on the GPU for a whole batch.
+ * mmz_align_cost: align [n][max_t][na][1500] fp16 (the decoder's alignment-head probabilities, token row i of clip s
+ * at position np + i) -> cost [n][max_t][1500] f32, row i at index i: rh(mean over the heads of the width-7 median of
+ * the per-column z-scores), bit-identical to src/align.rs:6-43 (the DTW runs on -cost). rows [n], cols [n] are device
+ * arrays: token rows (<= max_t - np) and frame columns (<= 1500) per clip. na <= 16. Asynchronous on `stream`.
+ * mmz_times_from_cost: the DTW over -cost [rows][ld] and the start time of each row (src/align.rs:44-63), on the
+ * host. */
+int mmz_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int max_t, int na, void* cost,
+                   void* stream);
+int mmz_times_from_cost(const float* cost, int rows, int cols, int ld, float* out);
 /* DTW over cost m [rows][cols]; writes the path into text, time (rows + cols entries each) and its length into
  * *len. src/align.rs:66-106. */
 int mmz_dtw(const double* m, int rows, int cols, int* text, int* time, int* len);
@@ -162,6 +172,9 @@ long long mmz_engine_allocated(mmz_engine* e);
 /* Kernels of the engine's kernel image launched so far (each graph replay counts every kernel of the captured step;
  * cuBLAS GEMMs are not counted). */
 long long mmz_engine_launches(mmz_engine* e);
+/* bytes the last mmz_engine_transcribe copied device -> host (tokens and the timestamp inputs). No reference
+ * counterpart. */
+unsigned long long mmz_engine_d2h_bytes(mmz_engine* e);
 
 #ifdef __cplusplus
 }

@@ -62,6 +62,8 @@ SIGNATURES = {
     "mmz_add_layernorm": (_I, [_P, _P, _P, _P, _P, _I, _I, _F, _P]),
     "mmz_jump_times": (_I, [_FP, _I, _I, _I, _I, _I, _FP]),
     "mmz_dtw": (_I, [_DP, _I, _I, _IP, _IP, _IP]),
+    "mmz_align_cost": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
     "mmz_log_mel": (_I, [_FP, _L, _I, _FP, _IP]),
     "mmz_log_mel_batch": (_I, [ctypes.POINTER(_FP), ctypes.POINTER(_L), _I, _I, _I, _FP, _IP]),
     "mmz_synth_clip": (_I, [_ULL, _FP, _L]),
@@ -79,6 +81,7 @@ SIGNATURES = {
     "mmz_engine_sync": (_I, [_P]),
     "mmz_engine_allocated": (_LL, [_P]),
     "mmz_engine_launches": (_LL, [_P]),
+    "mmz_engine_d2h_bytes": (_ULL, [_P]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():
@@ -214,6 +217,23 @@ def jump_times(w, cols, width=7):
     rows, heads, cols_full = w.shape
     out = np.zeros(rows, np.float32)
     _check(lib.mmz_jump_times(_fp(w), rows, heads, cols_full, cols, width, _fp(out)), "jump_times")
+    return out
+
+
+def align_cost(align, rows, cols, np_, max_t, na, cost, n=None, stream=None):
+    """src/align.rs:6-43 on the GPU: align fp16 [n][max_t][na][1500] -> cost f32 [n][max_t][1500] (row i of clip s
+    from position np_ + i). rows, cols: int32 device arrays [n]."""
+    n = n if n is not None else rows.shape[0]
+    _check(lib.mmz_align_cost(_ptr(align), _ptr(rows), _ptr(cols), n, np_, max_t, na, _ptr(cost), _stream(stream)),
+           "align_cost")
+
+
+def times_from_cost(cost, cols):
+    """src/align.rs:44-63: float32 cost [rows][ld] (DTW over -cost) -> float32 [rows] start times (s)."""
+    cost = np.ascontiguousarray(cost, dtype=np.float32)
+    rows, ld = cost.shape
+    out = np.zeros(rows, np.float32)
+    _check(lib.mmz_times_from_cost(_fp(cost), rows, cols, ld, _fp(out)), "times_from_cost")
     return out
 
 

@@ -93,6 +93,17 @@ int mmz_jump_times(const float* w, int rows, int heads, int cols_full, int cols,
     return 0;
 }
 
+int mmz_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int max_t, int na, void* cost,
+                   void* stream) {
+    return launch_align_cost(align, rows, cols, n, np, max_t, na, cost, S(stream));
+}
+
+int mmz_times_from_cost(const float* cost, int rows, int cols, int ld, float* out) {
+    if (rows < 1 || cols < 0 || ld < cols) return fail("times_from_cost: bad shape (cols <= ld)");
+    times_from_cost(cost, rows, cols, ld, out);
+    return 0;
+}
+
 int mmz_dtw(const double* m, int rows, int cols, int* text, int* time, int* len) {
     if (rows < 0 || cols < 0) return fail("dtw: bad shape");
     *len = dtw(m, rows, cols, text, time);
@@ -186,5 +197,6 @@ int mmz_engine_sync(mmz_engine* e) {
 }
 long long mmz_engine_allocated(mmz_engine* e) { return e ? (long long)e->e->allocated() : 0; }
 long long mmz_engine_launches(mmz_engine* e) { return e ? e->e->launches() : 0; }
+unsigned long long mmz_engine_d2h_bytes(mmz_engine* e) { return e ? e->e->last_d2h_bytes() : 0; }
 
 }  // extern "C"

@@ -393,6 +393,14 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         stat_ = part_ = nullptr;
     }
     align_ = H(b * mt * na * TENC_);
+    if (k_->native()) {
+        cost_ = (float*)alloc(b * mt * TENC_ * 4);
+        rc_ = (int*)alloc(b * 2 * 4);
+        if (!cost_ || !rc_) {
+            err_ = "device memory allocation failed";
+            return;
+        }
+    }
     for (void* p : {s_, mel_, (void*)mel32_, x1_, h1_, x2_, ex_, eh_, eqkv_, eatt_, ef_, xkv_buf_, (void*)tok_, (void*)done_, (void*)ctr_,
                     x_, hb_, att_, dout_, dbias_, logits_, kc_, vc_, align_})
         if (!p) {
@@ -707,41 +715,80 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
         nrows[s] = std::max(0, ns - 1 - np);
         total += (size_t)nrows[s] * row;
     }
-    std::vector<uint16_t> a16(total);
-    size_t off = 0;
-    for (int s = 0; s < n; s++) {
-        if (nrows[s] > 0)
-            CUDA_CK(cudaMemcpyAsync(a16.data() + off, (char*)align_ + 2 * ((size_t)s * mt + np) * row,
-                                    (size_t)nrows[s] * row * 2, cudaMemcpyDeviceToHost, st_));
-        off += (size_t)nrows[s] * row;
-    }
-    CUDA_CK(cudaStreamSynchronize(st_));
     if (threads < 1) threads = (int)std::max(1u, std::thread::hardware_concurrency());
     threads = std::min(threads, n);
-    std::vector<size_t> starts(n);
-    for (int s = 0, o = 0; s < n; s++) {
-        starts[s] = o;
-        o += nrows[s] * row;
-    }
-    auto work = [&](int w) {
-        std::vector<float> wf;
-        for (int s = w; s < n; s += threads) {
-            float* ts = times + (size_t)s * mt;
-            std::fill(ts, ts + mt, 0.f);
-            lens[s] = nseq[s];
-            const int rows = nrows[s];
-            if (rows <= 0) continue;
-            wf.resize((size_t)rows * row);
-            const uint16_t* src = a16.data() + starts[s];
-            for (size_t i = 0; i < wf.size(); i++) wf[i] = h2f(src[i]);
-            jump_times(wf.data(), rows, na, TENC_, frames[s] / 2, 7, ts + np);
-            ts[nseq[s] - 1] = ts[np + rows - 1];
+    d2h_bytes_ = (size_t)n * mt * 4;
+    if (k_->native()) {
+        // the DTW cost of every clip on the GPU (align.rs:6-43), then only 4 bytes per (row, frame) to the host
+        std::vector<int> rc(2 * (size_t)n);
+        for (int s = 0; s < n; s++) {
+            rc[s] = nrows[s];
+            rc[n + s] = frames[s] / 2;
         }
-    };
-    std::vector<std::thread> th;
-    for (int w = 1; w < threads; w++) th.emplace_back(work, w);
-    work(0);
-    for (auto& t : th) t.join();
+        CUDA_CK(cudaMemcpyAsync(rc_, rc.data(), rc.size() * 4, cudaMemcpyHostToDevice, st_));
+        CK(launch_align_cost(align_, rc_, rc_ + n, n, np, mt, na, cost_, st_));
+        k_->launches++;
+        std::vector<float> ch((size_t)n * mt * TENC_);
+        for (int s = 0; s < n; s++)
+            if (nrows[s] > 0) {
+                const size_t off = (size_t)s * mt * TENC_;
+                CUDA_CK(cudaMemcpyAsync(ch.data() + off, cost_ + off, (size_t)nrows[s] * TENC_ * 4,
+                                        cudaMemcpyDeviceToHost, st_));
+                d2h_bytes_ += (size_t)nrows[s] * TENC_ * 4;
+            }
+        CUDA_CK(cudaStreamSynchronize(st_));
+        auto work = [&](int w) {
+            for (int s = w; s < n; s += threads) {
+                float* ts = times + (size_t)s * mt;
+                std::fill(ts, ts + mt, 0.f);
+                lens[s] = nseq[s];
+                const int rows = nrows[s];
+                if (rows <= 0) continue;
+                times_from_cost(ch.data() + (size_t)s * mt * TENC_, rows, frames[s] / 2, TENC_, ts + np);
+                ts[nseq[s] - 1] = ts[np + rows - 1];
+            }
+        };
+        std::vector<std::thread> th;
+        for (int w = 1; w < threads; w++) th.emplace_back(work, w);
+        work(0);
+        for (auto& t : th) t.join();
+    } else {
+        // the reference's path: every recorded probability to the host, jump_times per clip there (align.rs:8-63)
+        std::vector<uint16_t> a16(total);
+        size_t off = 0;
+        for (int s = 0; s < n; s++) {
+            if (nrows[s] > 0)
+                CUDA_CK(cudaMemcpyAsync(a16.data() + off, (char*)align_ + 2 * ((size_t)s * mt + np) * row,
+                                        (size_t)nrows[s] * row * 2, cudaMemcpyDeviceToHost, st_));
+            off += (size_t)nrows[s] * row;
+        }
+        d2h_bytes_ += total * 2;
+        CUDA_CK(cudaStreamSynchronize(st_));
+        std::vector<size_t> starts(n);
+        for (int s = 0, o = 0; s < n; s++) {
+            starts[s] = o;
+            o += nrows[s] * row;
+        }
+        auto work = [&](int w) {
+            std::vector<float> wf;
+            for (int s = w; s < n; s += threads) {
+                float* ts = times + (size_t)s * mt;
+                std::fill(ts, ts + mt, 0.f);
+                lens[s] = nseq[s];
+                const int rows = nrows[s];
+                if (rows <= 0) continue;
+                wf.resize((size_t)rows * row);
+                const uint16_t* src = a16.data() + starts[s];
+                for (size_t i = 0; i < wf.size(); i++) wf[i] = h2f(src[i]);
+                jump_times(wf.data(), rows, na, TENC_, frames[s] / 2, 7, ts + np);
+                ts[nseq[s] - 1] = ts[np + rows - 1];
+            }
+        };
+        std::vector<std::thread> th;
+        for (int w = 1; w < threads; w++) th.emplace_back(work, w);
+        work(0);
+        for (auto& t : th) t.join();
+    }
     auto t3 = clk::now();
     if (stage_s) {
         stage_s[0] = std::chrono::duration<double>(t1 - t0).count();

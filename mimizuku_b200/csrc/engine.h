@@ -76,6 +76,7 @@ class Engine {
     // GEMMs are not counted)
     long long launches() const;
     long long step_launches() const { return step_launches_; }
+    size_t last_d2h_bytes() const { return d2h_bytes_; }
 
    private:
     int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
@@ -123,6 +124,9 @@ class Engine {
     // encoder scratch for eg clips, decoder state for bmax sequences (model.rs:289-321)
     void *mel_, *x1_, *h1_, *x2_, *ex_, *eh_, *eqkv_, *eatt_, *ef_;
     void *xkv_buf_, *x_, *hb_, *att_, *dout_, *dbias_, *logits_, *kc_, *vc_, *s_, *stat_, *part_, *align_;
+    float* cost_ = nullptr;  // native image: the token-timestamp DTW cost [bmax][max_t][1500], reduced on the GPU
+    int* rc_ = nullptr;      // native image: token rows and frame columns per clip for the cost kernel
+    size_t d2h_bytes_ = 0;   // bytes the last transcribe copied device -> host
     int *tok_, *done_, *ctr_, *aslot_;
     unsigned char *sup_;
     float* mel32_;

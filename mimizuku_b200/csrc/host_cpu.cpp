@@ -256,8 +256,19 @@ void jump_times(const float* w, int rows, int heads, int cols_full, int cols, in
             }
         }
     }
+    for (size_t k = 0; k < avg.size(); k++) avg[k] = rh(avg[k] / (float)heads);
+    times_from_cost(avg.data(), rows, cols, cols, out);
+}
+
+// src/align.rs:44-63: the DTW over -cost and the start time of each token row
+void times_from_cost(const float* cost, int rows, int cols, int ld, float* out) {
+    if (cols == 0) {
+        std::fill(out, out + rows, 0.f);
+        return;
+    }
     std::vector<double> m((size_t)rows * cols);
-    for (size_t k = 0; k < m.size(); k++) m[k] = -(double)rh(avg[k] / (float)heads);
+    for (int i = 0; i < rows; i++)
+        for (int j = 0; j < cols; j++) m[(size_t)i * cols + j] = -(double)cost[(size_t)i * ld + j];
     std::vector<int> text(rows + cols + 2), time(rows + cols + 2);
     const int n = dtw(m.data(), rows, cols, text.data(), time.data());
     int k_out = 0;

@@ -18,6 +18,9 @@ float rh(float x);
 
 int dtw(const double* m, int rows, int cols, int* text, int* time);
 void jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out);
+// src/align.rs:44-63 alone: cost [rows][ld] holds rh(mean over heads of the median-filtered z-scores) (the DTW runs
+// on -cost); writes rows start times
+void times_from_cost(const float* cost, int rows, int cols, int ld, float* out);
 
 struct MelBank {
     int n_mels;

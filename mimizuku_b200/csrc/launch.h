@@ -48,6 +48,10 @@ int launch_layernorm(const void* x, const void* w, const void* b, void* out, int
 int launch_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
                          cudaStream_t st);
 
+// the DTW cost of the token timestamps for a batch of clips (align.cu)
+int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,
+                      cudaStream_t st);
+
 // engine-side elementwise and token kernels (misc.cu)
 int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,
                  cudaStream_t st);

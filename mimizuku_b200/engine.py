@@ -142,3 +142,8 @@ class Engine:
     def launches(self):
         """Kernels of the engine's kernel image launched so far (graph replays included, cuBLAS not)."""
         return lib.mmz_engine_launches(self._h)
+
+    @property
+    def d2h_bytes(self):
+        """Bytes the last transcribe copied device -> host."""
+        return lib.mmz_engine_d2h_bytes(self._h)

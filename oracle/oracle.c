@@ -368,11 +368,9 @@ static void sort7(float* v, int n) {
 }
 
 /* src/align.rs:6-63 */
-void orc_jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out) {
-    if (cols == 0) {
-        for (int i = 0; i < rows; i++) out[i] = 0.f;
-        return;
-    }
+/* src/align.rs:6-43 up to the DTW cost: cost[i * cols + j] = rh(mean over heads of the width-wide median (reflect
+   padding, total order) of the per-column z-scores) -- the DTW runs on -cost. */
+void orc_align_cost(const float* w, int rows, int heads, int cols_full, int cols, int width, float* cost) {
 #define AT(i, a, j) w[((long)(i) * heads + (a)) * cols_full + (j)]
     float* avg = (float*)calloc((size_t)rows * cols, sizeof(float));
     float* z = (float*)calloc((size_t)rows * cols, sizeof(float));
@@ -411,8 +409,19 @@ void orc_jump_times(const float* w, int rows, int heads, int cols_full, int cols
         }
     }
 #undef AT
+    for (long k = 0; k < (long)rows * cols; k++) cost[k] = orc_rh(avg[k] / (float)heads);
+    free(avg); free(z);
+}
+
+/* src/align.rs:44-63: DTW over -cost ([rows][cols], row stride ld) and the start time of each token row */
+void orc_times_from_cost(const float* cost, int rows, int cols, int ld, float* out) {
+    if (cols == 0) {
+        for (int i = 0; i < rows; i++) out[i] = 0.f;
+        return;
+    }
     double* m = (double*)malloc(sizeof(double) * (size_t)rows * cols);
-    for (long k = 0; k < (long)rows * cols; k++) m[k] = -(double)orc_rh(avg[k] / (float)heads);
+    for (int i = 0; i < rows; i++)
+        for (int j = 0; j < cols; j++) m[(long)i * cols + j] = -(double)cost[(long)i * ld + j];
     int* text = (int*)malloc(sizeof(int) * (size_t)(rows + cols + 2));
     int* time = (int*)malloc(sizeof(int) * (size_t)(rows + cols + 2));
     int n = orc_dtw(m, rows, cols, text, time);
@@ -421,5 +430,16 @@ void orc_jump_times(const float* w, int rows, int heads, int cols_full, int cols
         if (k == 0 || text[k] != text[k - 1]) out[k_out++] = (float)((double)time[k] * 0.02);
     float last = k_out > 0 ? out[k_out - 1] : 0.f;
     for (; k_out < rows; k_out++) out[k_out] = last;
-    free(avg); free(z); free(m); free(text); free(time);
+    free(m); free(text); free(time);
+}
+
+void orc_jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out) {
+    if (cols == 0) {
+        for (int i = 0; i < rows; i++) out[i] = 0.f;
+        return;
+    }
+    float* cost = (float*)malloc(sizeof(float) * (size_t)rows * cols);
+    orc_align_cost(w, rows, heads, cols_full, cols, width, cost);
+    orc_times_from_cost(cost, rows, cols, cols, out);
+    free(cost);
 }

@@ -63,6 +63,9 @@ void orc_cross_attn_f64(const uint16_t* q, const uint16_t* kv, double* out, doub
 int orc_dtw(const double* m, int rows, int cols, int* text, int* time);
 /* src/align.rs:8-63: w [rows][heads][cols_full]; writes rows start times. */
 void orc_jump_times(const float* w, int rows, int heads, int cols_full, int cols, int width, float* out);
+/* the two halves of orc_jump_times: the DTW cost (align.rs:6-43) and the DTW with the token start times (:44-63) */
+void orc_align_cost(const float* w, int rows, int heads, int cols_full, int cols, int width, float* cost);
+void orc_times_from_cost(const float* cost, int rows, int cols, int ld, float* out);
 
 #ifdef __cplusplus
 }

@@ -40,6 +40,8 @@ def _load():
         "orc_cross_attn_f64": (None, [_U16P, _U16P, _DP, _DP, _IP, _I, _I, _I, _I]),
         "orc_dtw": (_I, [_DP, _I, _I, _IP, _IP]),
         "orc_jump_times": (None, [_FP, _I, _I, _I, _I, _I, _FP]),
+        "orc_align_cost": (None, [_FP, _I, _I, _I, _I, _I, _FP]),
+        "orc_times_from_cost": (None, [_FP, _I, _I, _I, _FP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -146,6 +148,23 @@ def jump_times(w, cols, width=7):
     rows, heads, cols_full = w.shape
     out = np.zeros(rows, np.float32)
     orc.orc_jump_times(fp(w), rows, heads, cols_full, cols, width, fp(out))
+    return out
+
+
+def align_cost(w, cols, width=7):
+    """w float32 [rows][heads][cols_full] -> cost float32 [rows][cols] (src/align.rs:6-43)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, heads, cols_full = w.shape
+    out = np.zeros((rows, cols), np.float32)
+    orc.orc_align_cost(fp(w), rows, heads, cols_full, cols, width, fp(out))
+    return out
+
+
+def times_from_cost(cost, cols):
+    cost = np.ascontiguousarray(cost, dtype=np.float32)
+    rows, ld = cost.shape
+    out = np.zeros(rows, np.float32)
+    orc.orc_times_from_cost(fp(cost), rows, cols, ld, fp(out))
     return out
 
 

@@ -96,6 +96,20 @@ def test_jump_times_product_is_the_oracle_bit_for_bit(rows, heads, cols_full, co
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+def test_times_from_cost_product_is_the_oracle_and_splits_jump_times():
+    rng = np.random.default_rng(5)
+    for rows, heads, cols_full, cols in [(1, 2, 40, 30), (7, 3, 60, 4), (30, 10, 1500, 1500), (223, 2, 1500, 999)]:
+        w = rng.random((rows, heads, cols_full)).astype(np.float16).astype(np.float32) * 0.01
+        w[:, :, ::13] = 0.0
+        cost = O.align_cost(w, cols)
+        t_split = O.times_from_cost(cost, cols)
+        assert np.array_equal(t_split.view(np.uint32), O.jump_times(w, cols).view(np.uint32))
+        padded = np.zeros((rows, cols_full), np.float32)  # a row stride wider than cols, as the engine's buffer
+        padded[:, :cols] = cost
+        padded[:, cols:] = 1e6  # never read
+        assert np.array_equal(m.times_from_cost(padded, cols).view(np.uint32), t_split.view(np.uint32))
+
+
 def test_dtw_product_is_the_oracle_with_ties():
     rng = np.random.default_rng(1)
     for rows, cols in [(1, 1), (1, 9), (9, 1), (12, 40), (40, 12), (64, 300)]:
