@@ -27,11 +27,17 @@ extern "C" {
 int mmz_init(int device);
 const char* mmz_last_error(void);
 /* Reads and clears the device status word of the current device: code[0] error (0 none, 1 wait timed out,
- * 2 misaligned shared memory, 3 bad argument), code[1] kernel (1 enc_flash, 2 self_attn, 3 cross_attn), code[2] site.
+ * 2 misaligned shared memory, 3 bad argument), code[1] kernel (1 enc_flash, 2 self_attn, 3 cross_attn, 4 layernorm,
+ * 5 dec_linear, 6 the wait self-test), code[2] site.
  * Synchronises the device. No reference counterpart (the reference has no in-kernel failure detection). */
 int mmz_status(int code[3]);
 /* Sets the bound on every in-kernel wait, in milliseconds (default 1000). */
 int mmz_set_wait_limit_ms(int device, int ms);
+/* Failure-detection self-test: launches a kernel that waits on a barrier nothing arrives on, with a limit of
+ * limit_ms (1..10000). Its bounded waits give up, record (1 = timeout, 6 = self-test, site) in the status word that
+ * mmz_status reads, and the kernel returns; the context stays usable. No reference counterpart (the reference has no
+ * in-kernel failure detection). */
+int mmz_selftest_wait(int limit_ms, void* stream);
 
 /* ---------------------------------------------------------------- fp16 helpers (src/gpu.rs:79-119) */
 
@@ -88,6 +94,14 @@ int mmz_layernorm(const void* x, const void* w, const void* b, void* out, int ro
  * src/model.rs:533-537). */
 int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
                       void* stream);
+
+/* Decoder linear layer at m <= 32 sequences: y[m][n] = rh(x[m][:k] . w[n][:k] + bias[n]) (fp16 in and out, fp32
+ * accumulation; bias may be NULL), then GELU when gelu != 0 (fc1 followed by gelu_inplace, kernels/whisper.cu:107-112). x [m][ldx],
+ * w [n][k], y [m][ldy]; k a multiple of 64, x and w 16-byte aligned. Replaces the decoder step's cuBLAS GEMMs onto
+ * the bias image (src/gpu.rs:208-247, src/model.rs:664-714); the summation order differs from cuBLAS's, so results
+ * agree to fp32 rounding before the final fp16 rounding. */
+int mmz_dec_linear(const void* x, int ldx, const void* w, const void* bias, void* y, int ldy, int m, int n, int k,
+                   int gelu, void* stream);
 
 /* ---------------------------------------------------------------- token timestamps (host, src/align.rs) */
 

@@ -49,6 +49,7 @@ SIGNATURES = {
     "mmz_last_error": (ctypes.c_char_p, []),
     "mmz_status": (_I, [_IP]),
     "mmz_set_wait_limit_ms": (_I, [_I, _I]),
+    "mmz_selftest_wait": (_I, [_I, _P]),
     "mmz_h2f": (_F, [ctypes.c_uint16]),
     "mmz_f2h": (ctypes.c_uint16, [_F]),
     "mmz_rh": (_F, [_F]),
@@ -63,6 +64,7 @@ SIGNATURES = {
     "mmz_jump_times": (_I, [_FP, _I, _I, _I, _I, _I, _FP]),
     "mmz_dtw": (_I, [_DP, _I, _I, _IP, _IP, _IP]),
     "mmz_align_cost": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
     "mmz_log_mel": (_I, [_FP, _L, _I, _FP, _IP]),
     "mmz_log_mel_batch": (_I, [ctypes.POINTER(_FP), ctypes.POINTER(_L), _I, _I, _I, _FP, _IP]),
@@ -126,6 +128,12 @@ def status():
     out = (ctypes.c_int * 3)()
     _check(lib.mmz_status(out), "mmz_status")
     return tuple(out)
+
+
+def selftest_wait(limit_ms, stream=None):
+    """Runs a kernel whose bounded waits run out on purpose (nothing arrives on its barrier); returns status()."""
+    _check(lib.mmz_selftest_wait(limit_ms, _stream(stream)), "mmz_selftest_wait")
+    return status()
 
 
 def set_wait_limit_ms(device, ms):
@@ -218,6 +226,15 @@ def jump_times(w, cols, width=7):
     out = np.zeros(rows, np.float32)
     _check(lib.mmz_jump_times(_fp(w), rows, heads, cols_full, cols, width, _fp(out)), "jump_times")
     return out
+
+
+def dec_linear(x, w, bias, y, gelu=False, m=None, stream=None):
+    """y[m][n] = rh(x[m] . w[n] + bias[n]) (GELU after when gelu) on the tensor cores; x [m][k], w [n][k], y [m][n]
+    fp16 device tensors, m <= 32."""
+    mm = m if m is not None else x.shape[0]
+    n, k = w.shape
+    _check(lib.mmz_dec_linear(_ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), mm, n, k,
+                              1 if gelu else 0, _stream(stream)), "dec_linear")
 
 
 def align_cost(align, rows, cols, np_, max_t, na, cost, n=None, stream=None):

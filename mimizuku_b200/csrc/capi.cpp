@@ -40,6 +40,8 @@ int mmz_status(int code[3]) {
     return 0;
 }
 
+int mmz_selftest_wait(int limit_ms, void* stream) { return launch_wait_selftest(limit_ms, S(stream)); }
+
 int mmz_set_wait_limit_ms(int device, int ms) {
     if (cudaSetDevice(device) != cudaSuccess) return fail("cudaSetDevice failed");
     DevCtx& c = dev_ctx();
@@ -91,6 +93,11 @@ int mmz_jump_times(const float* w, int rows, int heads, int cols_full, int cols,
         return fail("jump_times: bad shape (odd width < 64, cols <= cols_full)");
     jump_times(w, rows, heads, cols_full, cols, width, out);
     return 0;
+}
+
+int mmz_dec_linear(const void* x, int ldx, const void* w, const void* bias, void* y, int ldy, int m, int n, int k,
+                   int gelu, void* stream) {
+    return launch_dec_linear(x, ldx, w, bias, y, ldy, m, n, k, gelu != 0, S(stream));
 }
 
 int mmz_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int max_t, int na, void* cost,

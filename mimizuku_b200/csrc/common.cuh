@@ -17,7 +17,7 @@ constexpr int NFR = 3000;   // mel frames (30 s)
 
 // ---- status word: [0] error code (first one wins), [1] kernel id, [2] detail
 enum : unsigned { ST_OK = 0, ST_TIMEOUT = 1, ST_MISALIGNED = 2, ST_BAD_ARG = 3 };
-enum : unsigned { K_ENC = 1, K_SELF = 2, K_CROSS = 3, K_LN = 4 };
+enum : unsigned { K_ENC = 1, K_SELF = 2, K_CROSS = 3, K_LN = 4, K_LIN = 5, K_SELFTEST = 6 };
 
 __device__ __forceinline__ void report(unsigned* status, unsigned code, unsigned kernel, unsigned detail) {
     if (status && atomicCAS(status, 0u, code) == 0u) {
@@ -164,6 +164,15 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// contiguous copy from this CTA's shared memory into the shared memory of a CTA of the cluster (dst and bar are
+// shared::cluster addresses from dsmem_addr), completing on that CTA's mbarrier; 16-byte aligned, size a multiple of 16
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     dst),
+                 "r"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -304,6 +313,17 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
             taddr),
         "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// 32 TMEM lanes x 16 consecutive 32-bit columns -> 16 registers per thread (waits for the load)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
         : "memory");
 }
 

@@ -51,6 +51,8 @@ class Kernels {
     // y = x W^T + bias for m <= 8 rows, or -2 when the image has no such kernel
     virtual int gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
                      cudaStream_t st) = 0;
+    // the logits product hb emb^T (model.rs:714-716) where the image has a kernel for it; -2: use cuBLAS
+    virtual int logits(const void*, int, const void*, void*, int, int, int, cudaStream_t) { return -2; }
 };
 
 // ---------------------------------------------------------------- native sm_100a kernels
@@ -108,6 +110,11 @@ class NativeKernels : public Kernels {
         return ++launches, launch_fill_bias_heads(y, bias, n8, st);
     }
     int gemv(const void*, int, const void*, void*, int, int, int, int, const void*, cudaStream_t) override { return -2; }
+    // split-K tensor-core product streaming the 133 MB embedding (m <= 32)
+    int logits(const void* hb, int d, const void* emb, void* out, int vocab, int b, int, cudaStream_t st) override {
+        if (b > 32) return -2;
+        return ++launches, launch_dec_linear(hb, d, emb, nullptr, out, vocab, b, vocab, d, false, st);
+    }
 };
 
 // ---------------------------------------------------------------- a fatbin with the reference's kernel names
@@ -613,7 +620,10 @@ int Engine::step(int b, int prompt_len) {
         CK(k_->add_layernorm(x_, ofc2, next, hb_, b, d, st_));
     }
     // logits = hb emb^T (no bias), then the greedy choice and the position counter
-    if (b <= 8) {
+    const int lr = k_->logits(hb_, d, emb_, logits_, dm_.vocab, b, d, st_);
+    if (lr == -1) return -1;
+    if (lr == 0) {
+    } else if (b <= 8) {
         int r = k_->gemv(hb_, d, emb_, logits_, dm_.vocab, b, dm_.vocab, d, nullptr, st_);
         if (r == -1) return -1;
         if (r == -2) CK(matmul(true, false, dm_.vocab, b, d, 1.f, emb_, d, 0, hb_, d, 0, 0.f, logits_, dm_.vocab, 0, 1));

@@ -32,7 +32,10 @@ int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], con
                  const uint32_t box[3], bool swizzle128);
 
 void init_dec_attn_attrs(DevCtx& c);
+// a kernel whose bounded wait runs out on purpose (runtime.cu)
+int launch_wait_selftest(int limit_ms, cudaStream_t st);
 void init_enc_attn_attrs();
+void init_dec_linear_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
 size_t cross_attn_scratch_bytes(int batch, int d);
@@ -47,6 +50,11 @@ int launch_layernorm(const void* x, const void* w, const void* b, void* out, int
                      cudaStream_t st);
 int launch_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
                          cudaStream_t st);
+
+// y[m][n] = rh(x[m] . W[n] + b[n]) (b may be null; GELU after the rounding when gelu), m <= 32, k a multiple of 64
+// (dec_linear.cu)
+int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, void* y, int ldy, int m, int n, int k,
+                      bool gelu, cudaStream_t st);
 
 // the DTW cost of the token timestamps for a batch of clips (align.cu)
 int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,

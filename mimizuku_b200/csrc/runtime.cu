@@ -72,6 +72,7 @@ DevCtx& dev_ctx() {
     if (const char* s = getenv("MMZ_WAIT_LIMIT_MS")) c.limit_ns = (unsigned long long)atoll(s) * 1000000ull;
     init_dec_attn_attrs(c);
     init_enc_attn_attrs();
+    init_dec_linear_attrs();
     cudaGetLastError();
     c.ok = true;
     c.err = "";
@@ -106,6 +107,30 @@ static int make_tmap(CUtensorMap* map, int rank, const void* base, const uint64_
                     swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : -1;
+}
+
+// Failure-detection self-test: a barrier nothing ever arrives on. Warp 0 waits with the suspending bounded wait, warp
+// 1 with the spinning one; the first to give up reports (ST_TIMEOUT, K_SELFTEST, 1 or 2) and makes the other stop.
+// The kernel then returns normally and the context stays usable.
+__global__ void wait_selftest_kernel(unsigned* status, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort;
+    if (threadIdx.x == 0) {
+        abort = 0;
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) mbar_wait(&bar, 0, &abort, limit_ns, status, K_SELFTEST, 1);
+    else mbar_wait_spin(&bar, 0, &abort, limit_ns, status, K_SELFTEST, 2);
+}
+
+int launch_wait_selftest(int limit_ms, cudaStream_t st) {
+    if (limit_ms < 1 || limit_ms > 10000) return fail("wait_selftest: 1 <= limit_ms <= 10000");
+    DevCtx& dc = dev_ctx();
+    if (!dc.ok) return fail(dc.err);
+    wait_selftest_kernel<<<1, 64, 0, st>>>(dc.status, (unsigned long long)limit_ms * 1000000ull);
+    return check_launch("wait_selftest");
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], const uint64_t strides[1],
