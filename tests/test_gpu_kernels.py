@@ -142,6 +142,29 @@ def test_cross_attn(cuda, ref, B, d, nl, layer, p):
     assert same > 0.999, same
 
 
+def test_cross_attn_scratch_shared_by_different_batches(cuda):
+    """One scratch buffer serves launches of different batch sizes (the engine's buffer is sized for its largest
+    batch): a small launch after a large one must not see the large launch's scores where its counters are."""
+    import mimizuku_b200 as m
+    torch = cuda
+    d, nl, layer, max_t, nh = 1280, 1, 0, 448, 20
+    scratch = torch.zeros(m.cross_attn_scratch_bytes(12, d), dtype=torch.uint8, device="cuda")
+    for B, seed in [(12, 1), (3, 2), (12, 3), (5, 4)]:
+        q, kv, aslot = _cross_inputs(B, d, nl, 4, seed=seed)
+        na = int((aslot >= 0).sum())
+        done = np.zeros(B, np.int32)
+        Q, KV, ASL, DONE = dev(q, torch), dev(kv, torch), dev(aslot, torch), dev(done, torch)
+        CTR = dev(np.array([9, 0, 0, 0], np.int32), torch)
+        ALN = torch.zeros(B, max_t, na, 1500, dtype=torch.float16, device="cuda")
+        OUT = torch.zeros(B, d, dtype=torch.float16, device="cuda")
+        m.cross_attn(Q, KV, OUT, ALN, ASL, CTR, DONE, layer, nl, d, na, max_t, scratch)
+        torch.cuda.synchronize()
+        assert m.status()[0] == 0
+        oo, _ = O.cross_attn(q, kv, np.zeros((B, max_t, na, 1500), np.float16), aslot, 9, done, layer, nl, d, na,
+                             max_t)
+        assert np.abs(f16(OUT) - oo.astype(np.float32)).max() <= 2 ** -9, B
+
+
 # ------------------------------------------------------------------ self-attention (kv_write folded in)
 
 @pytest.mark.parametrize("B,d,p", [(1, 384, 0), (3, 384, 1), (3, 384, 62), (2, 1280, 64), (4, 1280, 127),
