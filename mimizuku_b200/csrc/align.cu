@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(AL_THREADS) align_cost_kernel(const h16* __res
                                                                 int na, float* __restrict__ cost) {
     __shared__ float mean_s[AL_MAXH][AL_THREADS], sd_s[AL_MAXH][AL_THREADS];
     __shared__ float zt[AL_ROWS][AL_THREADS];
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const int s = blockIdx.y, t = threadIdx.x;
     const int rows = min(rows_of[s], mt - np), cols = min(cols_of[s], TENC);
     const int j0 = blockIdx.x * AL_COLS;
@@ -121,8 +122,9 @@ int launch_align_cost(const void* align, const int* rows, const int* cols, int n
     DevCtx& dc = dev_ctx();
     if (!dc.ok) return fail(dc.err);
     dim3 grid((TENC + AL_COLS - 1) / AL_COLS, n);
-    align_cost_kernel<<<grid, AL_THREADS, 0, st>>>((const h16*)align, rows, cols, np, mt, na, (float*)cost);
-    return check_launch("align_cost");
+    return check_pdl(launch_pdl(align_cost_kernel, grid, dim3(AL_THREADS), 0, st, (const h16*)align, rows, cols, np, mt,
+                                na, (float*)cost),
+                     "align_cost");
 }
 
 }  // namespace mmz

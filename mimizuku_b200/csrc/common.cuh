@@ -38,6 +38,15 @@ __device__ __forceinline__ uint64_t globaltimer() {
     return t;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched as a programmatic dependent (launch_pdl) may start while the previous kernel of the stream is
+// still running; griddep_wait blocks until that kernel has completed and its memory is visible (a no-op otherwise).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// lets the next kernel, if launched as a programmatic dependent, be scheduled once every CTA of this one has run this
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(128)
                      unsigned long long limit_ns) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     SelfSmem& s = *reinterpret_cast<SelfSmem*>(smem_raw);
+    griddep_wait();  // launched as a programmatic dependent of the qkv projection
     const int hh = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
     const int w = t >> 5, lane = t & 31;
     const int p = ctr[0], L = p + 1;
@@ -169,11 +170,6 @@ __global__ void __launch_bounds__(128)
 //   cross_combine_kernel  waits for the P.V kernel the same way and sums the 24 partials in chunk order
 // Scratch per launch: S [B][heads][1500] f32, stat [B][heads][24] float2, part [B][heads][24][64] f32.
 
-__device__ __forceinline__ void griddep_launch_dependents() {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
 struct XScratch {
     float* S;
     float2* stat;
@@ -212,6 +208,7 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
     __shared__ float qs[HD];
     __shared__ float sc[XPER];
     griddep_launch_dependents();  // the P.V kernel may start its V copies as soon as every CTA here is resident
+    griddep_wait();               // launched as a programmatic dependent of the q projection
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
     const int nh = d / HD, bh = b * nh + hh;
     if (done[b]) return;
@@ -378,8 +375,10 @@ int launch_cross_attn(const void* q, const void* kv, void* out, void* align, con
     if (!dc.ok) return fail(dc.err);
     XScratch xs = cross_scratch(scratch, batch, d / HD);
     dim3 grid(XCL, d / HD, batch);
-    cross_scores_kernel<<<grid, 128, 0, st>>>((const h16*)q, (const h16*)kv, xs, done, layer, nl, d);
-    if (check_launch("cross_scores")) return -1;
+    if (check_pdl(launch_pdl(cross_scores_kernel, grid, dim3(128), 0, st, (const h16*)q, (const h16*)kv, xs, done,
+                             layer, nl, d),
+                  "cross_scores"))
+        return -1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(128, 1, 1);
@@ -414,9 +413,9 @@ int launch_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* 
     if (make_tmap_2d(&km, kc, dims, strides, box, false) || make_tmap_2d(&vm, vc, dims, strides, box, false))
         return fail("self_attn: cuTensorMapEncodeTiled failed");
     dim3 grid(d / HD, batch);
-    self_attn_kernel<<<grid, 128, sizeof(SelfSmem), st>>>(km, vm, (const h16*)qkv, (h16*)kc, (h16*)vc, (h16*)out, ctr,
-                                                          done, maxT, d, dc.status, dc.limit_ns);
-    return check_launch("self_attn");
+    return check_pdl(launch_pdl(self_attn_kernel, grid, dim3(128), sizeof(SelfSmem), st, km, vm, (const h16*)qkv,
+                                (h16*)kc, (h16*)vc, (h16*)out, ctr, done, maxT, d, dc.status, dc.limit_ns),
+                     "self_attn");
 }
 
 int launch_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch, int maxT, int d, cudaStream_t st) {

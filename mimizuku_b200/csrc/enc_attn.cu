@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         return;
     }
     volatile int* abort = &s.abort;
+    griddep_wait();  // launched as a programmatic dependent of the qkv projection
     if (threadIdx.x == 0) {
         s.abort = 0;
         mbar_init(&s.bar_q, 1);
@@ -319,8 +320,9 @@ int launch_enc_flash(const void* qkv, void* out, int groups, int d, cudaStream_t
     const uint32_t box[3] = {HD, BM, 1};
     if (make_tmap_3d(&map, qkv, dims, strides, box, true)) return fail("enc_flash: cuTensorMapEncodeTiled failed");
     dim3 grid(NQT, d / HD, groups);
-    enc_flash_kernel<<<grid, NTHREADS, sizeof(Smem), st>>>(map, (h16*)out, d, dc.status, dc.limit_ns);
-    return check_launch("enc_flash");
+    return check_pdl(launch_pdl(enc_flash_kernel, grid, dim3(NTHREADS), sizeof(Smem), st, map, (h16*)out, d, dc.status,
+                                dc.limit_ns),
+                     "enc_flash");
 }
 
 void init_enc_attn_attrs() {

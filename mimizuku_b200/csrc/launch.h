@@ -31,6 +31,26 @@ int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], con
 int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
                  const uint32_t box[3], bool swizzle128);
 
+// Launches `kernel` as a programmatic dependent of the previous kernel in the stream, so that its launch overlaps that
+// kernel's tail; the kernel runs griddep_wait() before it touches memory.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+// launch_pdl, then the same check as check_launch
+int check_pdl(cudaError_t e, const char* what);
+
 void init_dec_attn_attrs(DevCtx& c);
 // a kernel whose bounded wait runs out on purpose (runtime.cu)
 int launch_wait_selftest(int limit_ms, cudaStream_t st);

@@ -36,6 +36,7 @@ template <int KP, bool ADD>
 __global__ void __launch_bounds__(128) ln_kernel(__half2* x, const __half2* dd, const __half2* w, const __half2* bias,
                                                  __half2* out, int n2, float eps) {
     __shared__ float part[4];
+    griddep_wait();  // launched as a programmatic dependent: its inputs come from the kernel before
     const long row = blockIdx.x;
     const int t = threadIdx.x;
     __half2* xr = x + row * n2;
@@ -92,14 +93,15 @@ static int launch_ln(void* x, const void* d, const void* w, const void* b, void*
     auto W = (const __half2*)w;
     auto B = (const __half2*)b;
     auto Y = (__half2*)out;
+    cudaError_t e = cudaSuccess;
     switch (kp) {
 #define MMZ_LN(K) \
-    case K: ln_kernel<K, ADD><<<rows, 128, 0, st>>>(X, D, W, B, Y, n2, eps); break;
+    case K: e = launch_pdl(ln_kernel<K, ADD>, dim3(rows), dim3(128), 0, st, X, D, W, B, Y, n2, eps); break;
         MMZ_LN(1) MMZ_LN(2) MMZ_LN(3) MMZ_LN(4) MMZ_LN(5) MMZ_LN(6) MMZ_LN(7) MMZ_LN(8)
 #undef MMZ_LN
         default: return fail("layernorm: dim too large");
     }
-    return check_launch(ADD ? "add_layernorm" : "layernorm");
+    return check_pdl(e, ADD ? "add_layernorm" : "layernorm");
 }
 
 int launch_layernorm(const void* x, const void* w, const void* b, void* out, int rows, int dim, float eps,

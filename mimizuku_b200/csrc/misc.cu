@@ -12,6 +12,7 @@ static inline unsigned blocks(long n, int per) { return (unsigned)((n + per - 1)
 // x[b] = h(tok_emb[tok[b, p]] + pos_emb[p]), p = ctr[0] (kernels/whisper.cu:303-307)
 __global__ void embed_kernel(const int* __restrict__ tok, const int* __restrict__ ctr, const h16* __restrict__ emb,
                              const h16* __restrict__ pe, h16* __restrict__ x, int maxT, int d) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const int b = blockIdx.x, p = ctr[0], t = tok[b * maxT + p];
     for (int c = threadIdx.x; c < d / 2; c += blockDim.x) {
         float2 e = __half22float2(reinterpret_cast<const __half2*>(emb + (long)t * d)[c]);
@@ -26,6 +27,7 @@ __global__ void embed_kernel(const int* __restrict__ tok, const int* __restrict_
 __global__ void __launch_bounds__(512) argmax_kernel(const h16* __restrict__ logits, int V, const unsigned char* sup,
                                                      int* tok, int* done, const int* ctr, int maxT, int prompt_len,
                                                      int eos, int bs1, int bs2) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     __shared__ float sv[16];
     __shared__ int si[16];
     const int b = blockIdx.x, p = ctr[0];
@@ -76,10 +78,11 @@ __global__ void __launch_bounds__(512) argmax_kernel(const h16* __restrict__ log
     }
 }
 
-__global__ void advance_kernel(int* ctr) { ctr[0] += 1; }
+__global__ void advance_kernel(int* ctr) { griddep_wait(); ctr[0] += 1; }
 
 // conv1 as a GEMM operand: X[g, t, ci * 3 + k] = mel[g, ci, t + k - 1] (kernels/whisper.cu:121-129)
 __global__ void im2col1_kernel(const h16* __restrict__ mel, h16* __restrict__ X, long n, int nm) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int j = (int)(i % (3 * nm));
@@ -90,6 +93,7 @@ __global__ void im2col1_kernel(const h16* __restrict__ mel, h16* __restrict__ X,
 
 // conv2 (stride 2) as a GEMM operand: X[g, t, ci * 3 + k] = h1[g, 2t + k - 1, ci] (kernels/whisper.cu:131-139)
 __global__ void im2col2_kernel(const h16* __restrict__ h1, h16* __restrict__ X, long n, int d) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int j = (int)(i % (3 * d));
@@ -101,6 +105,7 @@ __global__ void im2col2_kernel(const h16* __restrict__ h1, h16* __restrict__ X, 
 // exact (erf) GELU over half2 pairs (kernels/whisper.cu:106-113)
 __device__ __forceinline__ float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 __global__ void gelu_kernel(__half2* x, long n2) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n2) return;
     const float2 v = __half22float2(x[i]);
@@ -109,6 +114,7 @@ __global__ void gelu_kernel(__half2* x, long n2) {
 
 // x[r, c] += pos[r % period, c] (kernels/whisper.cu:115-119)
 __global__ void add_pos_kernel(h16* x, const h16* __restrict__ pos, long rows, int n, int period) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows * n) return;
     const long r = i / n;
@@ -118,6 +124,7 @@ __global__ void add_pos_kernel(h16* x, const h16* __restrict__ pos, long rows, i
 
 // rows of an output with row stride ld <- bias (kernels/whisper.cu:92-97), 8 halves per thread
 __global__ void fill_bias_kernel(h16* y, const h16* __restrict__ bias, long rows, int n, long ld) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x, n8 = n / 8;
     if (i >= rows * n8) return;
     const long r = i / n8;
@@ -127,6 +134,7 @@ __global__ void fill_bias_kernel(h16* y, const h16* __restrict__ bias, long rows
 
 // bias of the head-contiguous cross k/v buffer: y[blk, j, c] = bias[blk * 64 + c] (kernels/whisper.cu:99-104)
 __global__ void fill_bias_heads_kernel(h16* y, const h16* __restrict__ bias, long n8) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n8) return;
     reinterpret_cast<uint4*>(y)[i] =
@@ -141,6 +149,7 @@ __device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 __global__ void fill_normal_kernel(h16* p, long n, unsigned long long seed, float mean, float std) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const uint64_t r = splitmix64(seed * 0x2545f4914f6cdd1dull + (uint64_t)i);
@@ -151,65 +160,67 @@ __global__ void fill_normal_kernel(h16* p, long n, unsigned long long seed, floa
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ src, h16* __restrict__ dst, long n) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) dst[i] = h(src[i]);
 }
 
 int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,
                  cudaStream_t st) {
-    embed_kernel<<<batch, 128, 0, st>>>(tok, ctr, (const h16*)emb, (const h16*)pe, (h16*)x, maxT, d);
-    return check_launch("embed");
+    return check_pdl(launch_pdl(embed_kernel, dim3(batch), dim3(128), 0, st, tok, ctr, (const h16*)emb, (const h16*)pe, (h16*)x, maxT, d),
+                     "embed");
 }
 
 int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
                       int batch, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) {
-    argmax_kernel<<<batch, 512, 0, st>>>((const h16*)logits, V, sup, tok, done, ctr, maxT, prompt_len, eos, bs1, bs2);
-    return check_launch("argmax_tok");
+    return check_pdl(launch_pdl(argmax_kernel, dim3(batch), dim3(512), 0, st, (const h16*)logits, V, sup, tok, done, ctr, maxT, prompt_len, eos, bs1, bs2),
+                     "argmax_tok");
 }
 
 int launch_advance(int* ctr, cudaStream_t st) {
-    advance_kernel<<<1, 1, 0, st>>>(ctr);
-    return check_launch("advance");
+    return check_pdl(launch_pdl(advance_kernel, dim3(1), dim3(1), 0, st, ctr),
+                     "advance");
 }
 
 int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) {
-    im2col1_kernel<<<blocks(n, 256), 256, 0, st>>>((const h16*)mel, (h16*)X, n, nm);
-    return check_launch("im2col1");
+    return check_pdl(launch_pdl(im2col1_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (const h16*)mel, (h16*)X, n, nm),
+                     "im2col1");
 }
 
 int launch_im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) {
-    im2col2_kernel<<<blocks(n, 256), 256, 0, st>>>((const h16*)h1, (h16*)X, n, d);
-    return check_launch("im2col2");
+    return check_pdl(launch_pdl(im2col2_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (const h16*)h1, (h16*)X, n, d),
+                     "im2col2");
 }
 
 int launch_gelu(void* x, long n, cudaStream_t st) {
-    gelu_kernel<<<blocks(n / 2, 256), 256, 0, st>>>((__half2*)x, n / 2);
-    return check_launch("gelu");
+    return check_pdl(launch_pdl(gelu_kernel, dim3(blocks(n / 2, 256)), dim3(256), 0, st, (__half2*)x, n / 2),
+                     "gelu");
 }
 
 int launch_add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) {
-    add_pos_kernel<<<blocks(rows * n, 256), 256, 0, st>>>((h16*)x, (const h16*)pos, rows, n, period);
-    return check_launch("add_pos");
+    return check_pdl(launch_pdl(add_pos_kernel, dim3(blocks(rows * n, 256)), dim3(256), 0, st, (h16*)x, (const h16*)pos, rows, n, period),
+                     "add_pos");
 }
 
 int launch_fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaStream_t st) {
-    fill_bias_kernel<<<blocks(rows * (n / 8), 256), 256, 0, st>>>((h16*)y, (const h16*)bias, rows, n, ld);
-    return check_launch("fill_bias");
+    return check_pdl(launch_pdl(fill_bias_kernel, dim3(blocks(rows * (n / 8), 256)), dim3(256), 0, st, (h16*)y,
+                                (const h16*)bias, rows, n, ld),
+                     "fill_bias");
 }
 
 int launch_fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) {
-    fill_bias_heads_kernel<<<blocks(n8, 256), 256, 0, st>>>((h16*)y, (const h16*)bias, n8);
-    return check_launch("fill_bias_heads");
+    return check_pdl(launch_pdl(fill_bias_heads_kernel, dim3(blocks(n8, 256)), dim3(256), 0, st, (h16*)y, (const h16*)bias, n8),
+                     "fill_bias_heads");
 }
 
 int launch_fill_normal(void* p, long n, unsigned long long seed, float mean, float std, cudaStream_t st) {
-    fill_normal_kernel<<<blocks(n, 256), 256, 0, st>>>((h16*)p, n, seed, mean, std);
-    return check_launch("fill_normal");
+    return check_pdl(launch_pdl(fill_normal_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (h16*)p, n, seed, mean, std),
+                     "fill_normal");
 }
 
 int launch_f32_to_f16(const float* src, void* dst, long n, cudaStream_t st) {
-    f32_to_f16_kernel<<<blocks(n, 256), 256, 0, st>>>(src, (h16*)dst, n);
-    return check_launch("f32_to_f16");
+    return check_pdl(launch_pdl(f32_to_f16_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, src, (h16*)dst, n),
+                     "f32_to_f16");
 }
 
 }  // namespace mmz

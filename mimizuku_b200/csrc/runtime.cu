@@ -36,6 +36,11 @@ int check_launch(const char* what) {
     return 0;
 }
 
+int check_pdl(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) return failf("%s: launch failed: %s", what, cudaGetErrorString(e));
+    return check_launch(what);
+}
+
 static std::mutex g_mu;
 static DevCtx g_ctx[64];
 
