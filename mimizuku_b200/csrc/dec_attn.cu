@@ -112,13 +112,22 @@ __global__ void __launch_bounds__(128)
             __syncthreads();
         }
         if (is_k) {
-            // scores: a warp per position, 2 elements per lane (:331-336)
-            for (int jj = w; jj < STILE && j0 + jj < L; jj += 4) {
-                float2 k2 = __half22float2(reinterpret_cast<const __half2*>(tile + jj * HD)[lane]);
-                float a = s.q[2 * lane] * k2.x + s.q[2 * lane + 1] * k2.y;
-                for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffff, a, o);
-                if (lane == 0) s.sc[j0 + jj] = rh(a);
+            // scores: a warp per position, 2 elements per lane (:331-336); the warp's 8 positions of the tile go
+            // through the butterfly together (independent chains, each in the reference's order)
+            float a[STILE / 4];
+#pragma unroll
+            for (int u = 0; u < STILE / 4; u++) {
+                const float2 k2 = __half22float2(reinterpret_cast<const __half2*>(tile + (w + 4 * u) * HD)[lane]);
+                a[u] = s.q[2 * lane] * k2.x + s.q[2 * lane + 1] * k2.y;
             }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < STILE / 4; u++) a[u] += __shfl_xor_sync(0xffffffff, a[u], o);
+            if (lane == 0)
+#pragma unroll
+                for (int u = 0; u < STILE / 4; u++)
+                    if (j0 + w + 4 * u < L) s.sc[j0 + w + 4 * u] = rh(a[u]);
         } else {
             if (i == ntile) {
                 // every score is in: the reference's block max and block sum (:338-344, block_max / block_sum :22-46)

@@ -19,14 +19,13 @@ __device__ __forceinline__ float xor_sum(float v) {
 }
 
 // block_sum of kernels/whisper.cu:22-33 for a 128-thread block: per-warp butterfly, then the butterfly over the
-// four warp sums, i.e. (w0 + w2) + (w1 + w3)
+// four warp sums, which is (w0 + w2) + (w1 + w3) (the other lanes add zeros); `part` is not reused within a launch,
+// so one barrier suffices
 __device__ __forceinline__ float block_sum128(float v, float* part) {
     v = xor_sum(v);
-    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
     __syncthreads();
-    if (l == 0) part[w] = v;
-    __syncthreads();
-    return xor_sum(l < 4 ? part[l] : 0.f);
+    return (part[0] + part[2]) + (part[1] + part[3]);
 }
 
 // KP = pairs per thread = ceil(n2 / 128); rows of n2 half2 pairs; ADD: x = h(x + d) first.
@@ -35,10 +34,17 @@ __device__ __forceinline__ float block_sum128(float v, float* part) {
 template <int KP, bool ADD>
 __global__ void __launch_bounds__(128) ln_kernel(__half2* x, const __half2* dd, const __half2* w, const __half2* bias,
                                                  __half2* out, int n2, float eps) {
-    __shared__ float part[4];
-    griddep_wait();  // launched as a programmatic dependent: its inputs come from the kernel before
+    __shared__ float part[2][4];
     const long row = blockIdx.x;
     const int t = threadIdx.x;
+    __half2 hw[KP], hb[KP];  // the parameters do not come from the kernel before: read them first
+#pragma unroll
+    for (int k = 0; k < KP; k++) {
+        const int i = t + 128 * k;
+        hw[k] = i < n2 ? w[i] : __float2half2_rn(0.f);
+        hb[k] = i < n2 ? bias[i] : __float2half2_rn(0.f);
+    }
+    griddep_wait();  // launched as a programmatic dependent: x and d come from the kernel before
     __half2* xr = x + row * n2;
     const __half2* dr = ADD ? dd + row * n2 : nullptr;
     __half2 hx[KP], hd[KP];
@@ -66,18 +72,18 @@ __global__ void __launch_bounds__(128) ln_kernel(__half2* x, const __half2* dd, 
             s += a.x + a.y;
         }
     }
-    const float mean = block_sum128(s, part) / (2 * n2);
+    const float mean = block_sum128(s, part[0]) / (2 * n2);
     float var = 0.f;
 #pragma unroll
     for (int k = 0; k < KP; k++)
         if (t + 128 * k < n2) var += (v[k].x - mean) * (v[k].x - mean) + (v[k].y - mean) * (v[k].y - mean);
-    const float rstd = rsqrtf(block_sum128(var, part) / (2 * n2) + eps);
+    const float rstd = rsqrtf(block_sum128(var, part[1]) / (2 * n2) + eps);
     __half2* yr = out + row * n2;
 #pragma unroll
     for (int k = 0; k < KP; k++) {
         const int i = t + 128 * k;
         if (i < n2) {
-            const float2 wv = __half22float2(w[i]), bv = __half22float2(bias[i]);
+            const float2 wv = __half22float2(hw[k]), bv = __half22float2(hb[k]);
             yr[i] = __floats2half2_rn((v[k].x - mean) * rstd * wv.x + bv.x, (v[k].y - mean) * rstd * wv.y + bv.y);
         }
     }
