@@ -10,8 +10,9 @@
 //
 // The array is shared by every call on a device and keeps the last call's contents; nothing in it needs to start at
 // zero (every value a call reads was written earlier in the same call). Calls that overlap on the GPU (other streams,
-// other threads) race on the array and must be serialised by the caller. The first call on a device resolves the array's device address (cudaGetSymbolAddress, with that
-// device current): make that first call before any stream capture.
+// other threads) race on the array and must be serialised by the caller. The first call on a device resolves the
+// array's device address (cudaGetSymbolAddress, with that device current): make that first call before any stream
+// capture.
 #include <mutex>
 
 #include "../../include/mimizuku_b200.h"

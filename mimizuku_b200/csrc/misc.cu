@@ -24,24 +24,43 @@ __global__ void embed_kernel(const int* __restrict__ tok, const int* __restrict_
 // Greedy choice of token p + 1 (kernels/whisper.cu:451-493): suppressed ids (sup[i] != 0, and bs1 / bs2 at the first
 // generated position) are skipped, ties go to the lower id, prompt positions stay, finished rows and rows with every
 // id suppressed get eos.
-__global__ void __launch_bounds__(512) argmax_kernel(const h16* __restrict__ logits, int V, const unsigned char* sup,
-                                                     int* tok, int* done, const int* ctr, int maxT, int prompt_len,
-                                                     int eos, int bs1, int bs2) {
+__device__ __forceinline__ void keep_best(float v, int i, float& best, int& bi) {
+    if (v > best || (v == best && i < bi)) {
+        best = v;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(1024) argmax_kernel(const h16* __restrict__ logits, int V, const unsigned char* sup,
+                                                      int* tok, int* done, const int* ctr, int maxT, int prompt_len,
+                                                      int eos, int bs1, int bs2) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
-    __shared__ float sv[16];
-    __shared__ int si[16];
+    __shared__ float sv[32];
+    __shared__ int si[32];
     const int b = blockIdx.x, p = ctr[0];
     if (p + 1 < prompt_len || p + 1 >= maxT) return;
     const bool first = p + 1 == prompt_len;
     const h16* lg = logits + (long)b * V;
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        if (sup[i] || (first && (i == bs1 || i == bs2))) continue;
-        const float v = f(lg[i]);
-        if (v > best || (v == best && i < bi)) {
-            best = v;
-            bi = i;
+    if ((V & 1) == 0) {
+        // even V: every row starts 4-byte aligned, so ids are scanned in pairs, several loads in flight per thread;
+        // each thread still visits its ids in increasing order, so ties keep the lower id
+        const __half2* lg2 = reinterpret_cast<const __half2*>(lg);
+        const unsigned short* sup2 = reinterpret_cast<const unsigned short*>(sup);
+        const int n2 = V / 2;
+#pragma unroll 4
+        for (int j = threadIdx.x; j < n2; j += blockDim.x) {
+            const float2 v = __half22float2(lg2[j]);
+            const unsigned short sp = sup2[j];
+            const int i = 2 * j;
+            if (!(sp & 0xff) && !(first && (i == bs1 || i == bs2))) keep_best(v.x, i, best, bi);
+            if (!(sp >> 8) && !(first && (i + 1 == bs1 || i + 1 == bs2))) keep_best(v.y, i + 1, best, bi);
+        }
+    } else {
+        for (int i = threadIdx.x; i < V; i += blockDim.x) {
+            if (sup[i] || (first && (i == bs1 || i == bs2))) continue;
+            keep_best(f(lg[i]), i, best, bi);
         }
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -167,13 +186,15 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ src, h16* __restrict
 
 int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,
                  cudaStream_t st) {
-    return check_pdl(launch_pdl(embed_kernel, dim3(batch), dim3(128), 0, st, tok, ctr, (const h16*)emb, (const h16*)pe, (h16*)x, maxT, d),
+    return check_pdl(launch_pdl(embed_kernel, dim3(batch), dim3(128), 0, st, tok, ctr, (const h16*)emb, (const h16*)pe,
+                                (h16*)x, maxT, d),
                      "embed");
 }
 
 int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
                       int batch, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) {
-    return check_pdl(launch_pdl(argmax_kernel, dim3(batch), dim3(512), 0, st, (const h16*)logits, V, sup, tok, done, ctr, maxT, prompt_len, eos, bs1, bs2),
+    return check_pdl(launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, st, (const h16*)logits, V, sup, tok, done,
+                                ctr, maxT, prompt_len, eos, bs1, bs2),
                      "argmax_tok");
 }
 
@@ -183,7 +204,8 @@ int launch_advance(int* ctr, cudaStream_t st) {
 }
 
 int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) {
-    return check_pdl(launch_pdl(im2col1_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (const h16*)mel, (h16*)X, n, nm),
+    return check_pdl(launch_pdl(im2col1_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (const h16*)mel, (h16*)X, n,
+                                nm),
                      "im2col1");
 }
 
@@ -198,7 +220,8 @@ int launch_gelu(void* x, long n, cudaStream_t st) {
 }
 
 int launch_add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) {
-    return check_pdl(launch_pdl(add_pos_kernel, dim3(blocks(rows * n, 256)), dim3(256), 0, st, (h16*)x, (const h16*)pos, rows, n, period),
+    return check_pdl(launch_pdl(add_pos_kernel, dim3(blocks(rows * n, 256)), dim3(256), 0, st, (h16*)x, (const h16*)pos,
+                                rows, n, period),
                      "add_pos");
 }
 
@@ -209,12 +232,14 @@ int launch_fill_bias(void* y, const void* bias, long rows, int n, long ld, cudaS
 }
 
 int launch_fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) {
-    return check_pdl(launch_pdl(fill_bias_heads_kernel, dim3(blocks(n8, 256)), dim3(256), 0, st, (h16*)y, (const h16*)bias, n8),
+    return check_pdl(launch_pdl(fill_bias_heads_kernel, dim3(blocks(n8, 256)), dim3(256), 0, st, (h16*)y,
+                                (const h16*)bias, n8),
                      "fill_bias_heads");
 }
 
 int launch_fill_normal(void* p, long n, unsigned long long seed, float mean, float std, cudaStream_t st) {
-    return check_pdl(launch_pdl(fill_normal_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (h16*)p, n, seed, mean, std),
+    return check_pdl(launch_pdl(fill_normal_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (h16*)p, n, seed, mean,
+                                std),
                      "fill_normal");
 }
 
