@@ -22,10 +22,12 @@ namespace mmz {
 
 // ============================================================================ cross-attention
 
-constexpr int XCL = 8;                        // CTAs per (sequence, head)
 constexpr int XCH = 64;                       // reference chunk (kernels/whisper.cu:360)
-constexpr int XPER = 3 * XCH;                 // positions per CTA: three reference chunks; 8 x 192 >= 1500
 constexpr int XNCH = (TENC + XCH - 1) / XCH;  // 24 chunks
+constexpr int XCPC = 3;                       // reference chunks per CTA (1: 66 us, 2: 51.1 us, 3: 50.6 us per layer)
+constexpr int XCL = XNCH / XCPC;              // CTAs per (sequence, head)
+constexpr int XPER = XCPC * XCH;              // positions per CTA
+static_assert(XNCH % XCPC == 0 && XCPC <= 4, "whole chunks per CTA, one warp per chunk for the statistics");
 
 // kv: [b][layer][k | v][head][1500][64] (kernels/whisper.cu:362-364)
 __device__ __forceinline__ long xkv_off(int b, int layer, int kv, int hh, int nl, int nh) {
@@ -253,13 +255,13 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
     __syncthreads();
     // chunk statistics, warp c for chunk c (kernels/whisper.cu:394-401)
     const int w = t >> 5, lane = t & 31;
-    if (w < 3) {
+    if (w < XCPC) {
         float a = sc[w * XCH + lane], b2 = sc[w * XCH + lane + 32];
         float m = fmaxf(a, b2);
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffff, m, o));
         float sm = (a == -INFINITY ? 0.f : expf(a - m)) + (b2 == -INFINITY ? 0.f : expf(b2 - m));
         for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffff, sm, o);
-        if (lane == 0) xs.stat[(long)bh * XNCH + r * 3 + w] = make_float2(m, sm);
+        if (lane == 0) xs.stat[(long)bh * XNCH + r * XCPC + w] = make_float2(m, sm);
     }
 }
 
@@ -272,8 +274,8 @@ __global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict_
     __shared__ __align__(128) h16 vs[XPER * HD];  // this CTA's V slice, bulk copies issued before the wait
     __shared__ float p[XPER];
     __shared__ float2 gs[XNCH];
-    __shared__ float red[3][16][HD];
-    __shared__ uint64_t bar[3];
+    __shared__ float red[XCPC][16][HD];
+    __shared__ uint64_t bar[XCPC];
     __shared__ int abort;
     griddep_launch_dependents();  // the combine kernel may be scheduled as soon as every CTA here is resident
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
@@ -284,9 +286,9 @@ __global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict_
     if (t == 0) {  // V does not depend on the scores: its copies are in flight before the wait
         abort = 0;
         const h16* V = kv + xkv_off(b, layer, 1, hh, nl, nh) + (long)j0 * HD;
-        for (int c = 0; c < 3; c++) mbar_init(&bar[c], 1);
+        for (int c = 0; c < XCPC; c++) mbar_init(&bar[c], 1);
         fence_mbar_init();
-        for (int c = 0; c < 3; c++) {
+        for (int c = 0; c < XCPC; c++) {
             const int nc = min(XCH, n - c * XCH);
             mbar_expect_tx(&bar[c], nc * HD * 2);
             bulk_g2s(vs + c * XCH * HD, V + (long)c * XCH * HD, nc * HD * 2, &bar[c]);
@@ -314,7 +316,7 @@ __global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict_
     __syncthreads();
     // P.V per chunk: 16 groups x 8 lanes, a lane owns 8 of the 64 columns (kernels/whisper.cu:421-438); the three
     // chunks' group sums meet in shared memory behind one barrier
-    for (int c = 0; c < 3; c++) {
+    for (int c = 0; c < XCPC; c++) {
         mbar_wait(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 4 + c);
         const int nc = min(XCH, n - c * XCH);
         float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -333,14 +335,14 @@ __global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict_
         for (int e = 0; e < 8; e++) red[c][grp][sub * 8 + e] = a[e];
     }
     __syncthreads();
-    for (int i = t; i < 3 * HD; i += 128) {
+    for (int i = t; i < XCPC * HD; i += 128) {
         const int c = i / HD, col = i % HD;
         float acc = 0.f;
         for (int g = 0; g < 16; g++) acc += red[c][g][col];
-        xs.part[((long)bh * XNCH + r * 3 + c) * HD + col] = acc;
+        xs.part[((long)bh * XNCH + r * XCPC + c) * HD + col] = acc;
     }
     if (t == 0 && abort)
-        for (int c = 0; c < 3; c++) mbar_wait(&bar[c], 0, nullptr, limit_ns, nullptr, 0, 0);
+        for (int c = 0; c < XCPC; c++) mbar_wait(&bar[c], 0, nullptr, limit_ns, nullptr, 0, 0);
 }
 
 // grid (heads, B), block 64; launched as a programmatic dependent of cross_pv_kernel: the 24 partials of a
