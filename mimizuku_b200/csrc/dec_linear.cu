@@ -6,8 +6,9 @@
 // is about keeping W moving, with the 5th-generation tensor cores doing the arithmetic:
 //   * W rows are the MMA's M side: a CTA owns 128 rows of W and computes the 128 x 32 tile of y^T in TMEM
 //     (tcgen05.mma kind::f16, M128 N32 K16, A = W tile, B = x tile, both K-major with 128-byte swizzle)
-//   * K is split across the CTAs of a thread-block cluster (up to 8), each streaming its share of the 64-wide K chunks
-//     through a 4-stage TMA ring (a 16 KB W tile and the 4 KB x tile per stage)
+//   * K is split across the CTAs of a thread-block cluster (up to 16), each streaming its share of the 64-wide K chunks
+//     through a 4-stage TMA ring (a 16 KB W tile and the 4 KB x tile per stage); launched as a programmatic
+//     dependent, a CTA issues its first W tiles before it waits for the kernel before (which x comes from)
 //   * the cluster's partial tiles meet in shared memory: every rank sends rank q its partials of the rows q owns with
 //     one bulk shared::cluster copy completing on q's mbarrier; q sums the slices in split order (deterministic),
 //     adds the bias, rounds to fp16 (GELU for fc1) and stores its rows of y
@@ -58,16 +59,21 @@ __global__ void __launch_bounds__(128) dec_linear_splitk_kernel(const __grid_con
     const int nch = k / BK, c0 = (int)((long)r * nch / S), c1 = (int)((long)(r + 1) * nch / S);
     volatile int* abort = &s.abort;
     const int R = BN / S;
-    const uint32_t slice_bytes = (uint32_t)(R * RP * 4);  // a multiple of 16 for every S in {1, 2, 4, 8}
+    const uint32_t slice_bytes = (uint32_t)(R * RP * 4);  // a multiple of 16 for every S in {1, 2, 4, 8, 16}
     int issued = 0;
-    auto issue = [&](int i) {
+    auto issue_w = [&](int i) {  // one stage: the byte count of both copies, then the W tile
         const int st = i % NS, c = c0 + i;
         mbar_expect_tx(&s.full[st], WT + XT);
         tma_load_2d(s.w[st], &wmap, c * BK, tile * BN, &s.full[st]);
+    };
+    auto issue_x = [&](int i) {
+        const int st = i % NS, c = c0 + i;
         tma_load_2d(s.x[st], &xmap, c * BK, 0, &s.full[st]);
     };
+    griddep_launch_dependents();  // the next kernel may be scheduled as soon as every CTA here runs
     if (threadIdx.x == 0) {
-        // the first copies go out before anything else
+        // the weight copies go out first: W does not depend on the kernel before, so with a programmatic dependent
+        // launch they overlap its tail
         s.abort = 0;
         for (int i = 0; i < NS; i++) {
             mbar_init(&s.full[i], 1);
@@ -78,9 +84,12 @@ __global__ void __launch_bounds__(128) dec_linear_splitk_kernel(const __grid_con
         fence_mbar_init();
         prefetch_tmap(&wmap);
         prefetch_tmap(&xmap);
-        for (; issued < NS && issued < c1 - c0; issued++) issue(issued);
+        for (; issued < NS && issued < c1 - c0; issued++) issue_w(issued);
         mbar_expect_tx(&s.got, slice_bytes * S);  // the partials of this rank's rows, one slice from every rank
     }
+    griddep_wait();  // x comes from the kernel before
+    if (threadIdx.x == 0)
+        for (int i = 0; i < issued; i++) issue_x(i);
     // the other ranks may send into this CTA's receive buffer once its barriers exist
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     if (warp == 0) {
@@ -97,7 +106,8 @@ __global__ void __launch_bounds__(128) dec_linear_splitk_kernel(const __grid_con
         for (int i = issued; i < c1 - c0; i++) {
             const int st = i % NS;
             if (!mbar_wait(&s.empty[st], ((i / NS) - 1) & 1, abort, limit_ns, status, K_LIN, 1)) break;
-            issue(i);
+            issue_w(i);
+            issue_x(i);
             issued = i + 1;
         }
         if (*abort)
@@ -177,21 +187,24 @@ int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, v
     const uint32_t xb[2] = {BK, BM};
     if (make_tmap_2d(&wm, w, wd, ws, wb, true) || make_tmap_2d(&xm, x, xd, xs, xb, true))
         return fail("dec_linear: cuTensorMapEncodeTiled failed");
+    // split K over a cluster of S CTAs: at least 2 chunks each, at most two CTAs per SM in all, 16 per cluster
     const int tiles = (n + BN - 1) / BN, nch = k / BK;
     int S = 1;
-    while (S < 8 && S * 2 <= nch && tiles * S < 2 * dc.sms) S *= 2;  // about two CTAs per SM, at most 8 per cluster
+    while (S < 16 && S * 4 <= nch && tiles * S * 2 <= 2 * dc.sms) S *= 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, tiles, 1);
     cfg.blockDim = dim3(128, 1, 1);
     cfg.dynamicSmemBytes = sizeof(Smem);
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = S;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // a programmatic dependent of the kernel before
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaError_t e = cudaLaunchKernelEx(&cfg, dec_linear_splitk_kernel, wm, xm, (const h16*)bias, (h16*)y, ldy, m, n, k,
                                        gelu ? 1 : 0, dc.status, dc.limit_ns);
     if (e != cudaSuccess) return failf("dec_linear: launch failed: %s", cudaGetErrorString(e));
@@ -200,6 +213,7 @@ int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, v
 
 void init_dec_linear_attrs() {
     cudaFuncSetAttribute(dec_linear_splitk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sizeof(Smem));
+    cudaFuncSetAttribute(dec_linear_splitk_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 
 }  // namespace mmz
