@@ -44,7 +44,7 @@ struct SelfSmem {
     h16 ring[SSTAGE][STILE * HD];  // 8 x 4 KB: K tiles, then V tiles, streamed through
     float q[HD];
     float sc[SMAXL];               // scores, then probabilities
-    float wred[4];
+    float wmax[4], wsum[4];        // per-warp partials of the block max and the block sum
     float red[HD];
     uint64_t full[SSTAGE];
     int abort;
@@ -133,20 +133,20 @@ __global__ void __launch_bounds__(128)
         } else {
             if (i == ntile) {
                 // every score is in: the reference's block max and block sum (:338-344, block_max / block_sum :22-46)
+                // (the butterfly over the four warp values is their max, and (w0 + w2) + (w1 + w3) for the sum)
                 __syncthreads();
                 float mx = -INFINITY;
                 for (int j = t; j < L; j += 128) mx = fmaxf(mx, s.sc[j]);
                 mx = warp_max(mx);
-                if (lane == 0) s.wred[w] = mx;
+                if (lane == 0) s.wmax[w] = mx;
                 __syncthreads();
-                m = warp_max(lane < 4 ? s.wred[lane] : -INFINITY);
+                m = fmaxf(fmaxf(s.wmax[0], s.wmax[1]), fmaxf(s.wmax[2], s.wmax[3]));
                 float e = 0.f;
                 for (int j = t; j < L; j += 128) e += expf(s.sc[j] - m);
                 e = warp_sum(e);
+                if (lane == 0) s.wsum[w] = e;
                 __syncthreads();
-                if (lane == 0) s.wred[w] = e;
-                __syncthreads();
-                sum = warp_sum(lane < 4 ? s.wred[lane] : 0.f);
+                sum = (s.wsum[0] + s.wsum[2]) + (s.wsum[1] + s.wsum[3]);
                 for (int j = t; j < L; j += 128) s.sc[j] = rh(expf(s.sc[j] - m) / sum);
                 __syncthreads();
             }
@@ -155,8 +155,10 @@ __global__ void __launch_bounds__(128)
             for (int jj = half; jj < STILE && j0 + jj < L; jj += 2)
                 acc += s.sc[j0 + jj] * f(tile[jj * HD + col]);
         }
-        __syncthreads();  // everyone is done with this stage
-        if (t == 0 && i + SSTAGE < total) issue(i + SSTAGE);
+        if (i + SSTAGE < total) {  // the stage is refilled: everyone must be done with it
+            __syncthreads();
+            if (t == 0) issue(i + SSTAGE);
+        }
     }
     // :350-352
     if (half == 1) s.red[col] = acc;

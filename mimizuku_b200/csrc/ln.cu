@@ -1,6 +1,7 @@
 // Residual add fused with LayerNorm, and plain LayerNorm, for sm_100a (kernels/whisper.cu:48-82 of the reference).
 //
-// One 128-thread block per row with the reference's thread mapping: thread t owns the half2 pairs t, t + 128, ...
+// One 128-thread block per row (a warp per row from 1024 rows on, below) with the reference's thread mapping: thread t
+// owns the half2 pairs t, t + 128, ...
 // (:51, :54-57), but keeps them in registers, so x (and d) are read from HBM once and x = h(x + d) and the normalised
 // row are written once; the reference block reads x again for each of its passes. Memory traffic per row is the
 // algorithmic minimum (4 x dim x 2 bytes for add_layernorm).
@@ -89,6 +90,81 @@ __global__ void __launch_bounds__(128) ln_kernel(__half2* x, const __half2* dd, 
     }
 }
 
+// The same computation with one warp per row, for many rows (the encoder's 12 000): lane l plays the reference's
+// threads l, l + 32, l + 64 and l + 96 (one per warp of the 128-thread block), keeps each one's sum in pair order,
+// runs the per-warp butterfly on each, and adds the four warp sums as (w0 + w2) + (w1 + w3): the reference's
+// arithmetic without a barrier or shared memory. Every load of the row is issued before the first store.
+template <int KP, bool ADD>
+__global__ void __launch_bounds__(128) ln_warp_kernel(__half2* x, const __half2* dd, const __half2* w,
+                                                      const __half2* bias, __half2* out, int rows, int n2,
+                                                      float eps) {
+    griddep_wait();  // launched as a programmatic dependent: x and d come from the kernel before
+    const long row = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int l = threadIdx.x & 31;
+    __half2* xr = x + row * n2;
+    const __half2* dr = ADD ? dd + row * n2 : nullptr;
+    __half2 hx[4][KP], hd[4][KP];
+#pragma unroll
+    for (int k = 0; k < KP; k++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int i = l + 32 * q + 128 * k;  // thread l + 32 q of the reference's block, its k-th pair
+            hx[q][k] = i < n2 ? xr[i] : __float2half2_rn(0.f);
+            if (ADD) hd[q][k] = i < n2 ? dr[i] : __float2half2_rn(0.f);
+        }
+    float2 v[4][KP];
+    float s[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        s[q] = 0.f;
+#pragma unroll
+        for (int k = 0; k < KP; k++) {
+            const int i = l + 32 * q + 128 * k;
+            v[q][k] = make_float2(0.f, 0.f);
+            if (i < n2) {
+                float2 a = __half22float2(hx[q][k]);
+                if (ADD) {
+                    const float2 b = __half22float2(hd[q][k]);
+                    const __half2 y = __floats2half2_rn(a.x + b.x, a.y + b.y);
+                    xr[i] = y;
+                    a = __half22float2(y);
+                }
+                v[q][k] = a;
+                s[q] += a.x + a.y;
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) s[q] = xor_sum(s[q]);
+    const float mean = ((s[0] + s[2]) + (s[1] + s[3])) / (2 * n2);
+    float var[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        var[q] = 0.f;
+#pragma unroll
+        for (int k = 0; k < KP; k++)
+            if (l + 32 * q + 128 * k < n2)
+                var[q] += (v[q][k].x - mean) * (v[q][k].x - mean) + (v[q][k].y - mean) * (v[q][k].y - mean);
+        var[q] = xor_sum(var[q]);
+    }
+    const float rstd = rsqrtf(((var[0] + var[2]) + (var[1] + var[3])) / (2 * n2) + eps);
+    __half2* yr = out + row * n2;
+#pragma unroll
+    for (int k = 0; k < KP; k++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int i = l + 32 * q + 128 * k;
+            if (i < n2) {
+                const float2 wv = __half22float2(w[i]), bv = __half22float2(bias[i]);
+                yr[i] = __floats2half2_rn((v[q][k].x - mean) * rstd * wv.x + bv.x,
+                                          (v[q][k].y - mean) * rstd * wv.y + bv.y);
+            }
+        }
+}
+
+constexpr int LN_WARP_ROWS = 1024;  // from this many rows on, a warp per row
+
 template <bool ADD>
 static int launch_ln(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
                      cudaStream_t st) {
@@ -100,9 +176,14 @@ static int launch_ln(void* x, const void* d, const void* w, const void* b, void*
     auto B = (const __half2*)b;
     auto Y = (__half2*)out;
     cudaError_t e = cudaSuccess;
+    const bool warp_rows = rows >= LN_WARP_ROWS && kp <= 5;  // larger rows would not fit in registers
+    const dim3 wgrid((rows + 3) / 4);
     switch (kp) {
-#define MMZ_LN(K) \
-    case K: e = launch_pdl(ln_kernel<K, ADD>, dim3(rows), dim3(128), 0, st, X, D, W, B, Y, n2, eps); break;
+#define MMZ_LN(K)                                                                                                   \
+    case K:                                                                                                         \
+        e = warp_rows ? launch_pdl(ln_warp_kernel<K, ADD>, wgrid, dim3(128), 0, st, X, D, W, B, Y, rows, n2, eps) \
+                      : launch_pdl(ln_kernel<K, ADD>, dim3(rows), dim3(128), 0, st, X, D, W, B, Y, n2, eps);      \
+        break;
         MMZ_LN(1) MMZ_LN(2) MMZ_LN(3) MMZ_LN(4) MMZ_LN(5) MMZ_LN(6) MMZ_LN(7) MMZ_LN(8)
 #undef MMZ_LN
         default: return fail("layernorm: dim too large");
