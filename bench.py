@@ -248,10 +248,11 @@ def main():
     steps_dec = np_ - 1 + NEW_TOKENS
     st = torch.cuda.ExternalStream(e.stream)
 
-    if args.impl == "native":  # the timestamp cost is reduced on the GPU (the reference does it on the host)
+    if args.impl == "native":  # the timestamp cost and DTW run on the GPU (the reference does them on the host)
         rc_dev = torch.tensor([NEW_TOKENS - 1] * CLIPS_PER_GPU + [int(f) // 2 for f in frames], dtype=torch.int32,
                               device="cuda")
         cost_dev = torch.empty((CLIPS_PER_GPU, cfg.max_t, 1500), dtype=torch.float32, device="cuda")
+        times_dev = torch.empty((CLIPS_PER_GPU, cfg.max_t), dtype=torch.float32, device="cuda")
 
     def gpu_pipeline():
         for g0 in range(0, CLIPS_PER_GPU, 8):
@@ -262,6 +263,8 @@ def main():
         if args.impl == "native":
             m.align_cost(e.buffer("align"), rc_dev[:CLIPS_PER_GPU], rc_dev[CLIPS_PER_GPU:], np_, cfg.max_t, e.na,
                          cost_dev, n=CLIPS_PER_GPU, stream=e.stream)
+            m.dtw_times(cost_dev, rc_dev[:CLIPS_PER_GPU], rc_dev[CLIPS_PER_GPU:], cfg.max_t, times_dev,
+                        n=CLIPS_PER_GPU, stream=e.stream)
 
     def barrier():
         if dist:
@@ -290,7 +293,7 @@ def main():
             gpu_pipeline()
         b.record(st)
         b.synchronize()
-    launches = e.launches - launches0 + (args.steps if args.impl == "native" else 0)  # + the cost kernels
+    launches = e.launches - launches0 + (2 * args.steps if args.impl == "native" else 0)  # + cost and DTW kernels
     t_dev = max_over_ranks(a.elapsed_time(b) * 1e-3)
     torch.cuda.synchronize()
     barrier()

@@ -113,10 +113,14 @@ int mmz_jump_times(const float* w, int rows, int heads, int cols_full, int cols,
  * at position np + i) -> cost [n][max_t][1500] f32, row i at index i: rh(mean over the heads of the width-7 median of
  * the per-column z-scores), bit-identical to src/align.rs:6-43 (the DTW runs on -cost). rows [n], cols [n] are device
  * arrays: token rows (<= max_t - np) and frame columns (<= 1500) per clip. na <= 16. Asynchronous on `stream`.
- * mmz_times_from_cost: the DTW over -cost [rows][ld] and the start time of each row (src/align.rs:44-63), on the
- * host. */
+ * mmz_dtw_times: the DTW over -cost and the start time of each token row (src/align.rs:44-106) for the whole batch
+ * on the GPU: cost [n][max_t][1500] as mmz_align_cost writes it, rows / cols the same device arrays, times [n][max_t]
+ * f32 (entry i < rows[s] = start of token row i in seconds, 0 past it), bit-identical to mmz_times_from_cost with
+ * ld = 1500. max_t <= 512. Asynchronous on `stream`.
+ * mmz_times_from_cost: the same DTW for one clip on the host (cost [rows][ld]). */
 int mmz_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int max_t, int na, void* cost,
                    void* stream);
+int mmz_dtw_times(const void* cost, const int* rows, const int* cols, int n, int max_t, void* times, void* stream);
 int mmz_times_from_cost(const float* cost, int rows, int cols, int ld, float* out);
 /* DTW over cost m [rows][cols]; writes the path into text, time (rows + cols entries each) and its length into
  * *len. src/align.rs:66-106. */

@@ -64,6 +64,7 @@ SIGNATURES = {
     "mmz_jump_times": (_I, [_FP, _I, _I, _I, _I, _I, _FP]),
     "mmz_dtw": (_I, [_DP, _I, _I, _IP, _IP, _IP]),
     "mmz_align_cost": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "mmz_dtw_times": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
     "mmz_log_mel": (_I, [_FP, _L, _I, _FP, _IP]),
@@ -243,6 +244,14 @@ def align_cost(align, rows, cols, np_, max_t, na, cost, n=None, stream=None):
     n = n if n is not None else rows.shape[0]
     _check(lib.mmz_align_cost(_ptr(align), _ptr(rows), _ptr(cols), n, np_, max_t, na, _ptr(cost), _stream(stream)),
            "align_cost")
+
+
+def dtw_times(cost, rows, cols, max_t, times, n=None, stream=None):
+    """src/align.rs:44-106 on the GPU for a batch: cost f32 [n][max_t][1500] (as align_cost writes it) -> times f32
+    [n][max_t] (row i < rows[s]: start time in seconds, 0 past it). rows, cols: int32 device arrays [n]."""
+    n = n if n is not None else rows.shape[0]
+    _check(lib.mmz_dtw_times(_ptr(cost), _ptr(rows), _ptr(cols), n, max_t, _ptr(times), _stream(stream)),
+           "dtw_times")
 
 
 def times_from_cost(cost, cols):

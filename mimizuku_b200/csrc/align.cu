@@ -4,11 +4,13 @@
 //   rounded to fp16), z = rh(rh(w - mean) / sd) (0 where sd = 0);
 //   per row: the width-7 median of z along the columns (reflect padding, f32 total order), summed over the heads in
 //   order; cost = rh(sum / heads).
-// The DTW itself (align.rs:44-106) is sequential per clip and stays on the host (times_from_cost), which now receives
-// 4 bytes per (row, column) instead of the 2 x heads bytes of the raw probabilities.
+// Then the DTW over -cost and the start time of each token row (align.rs:44-106), one CTA per clip: the cost table is
+// filled along anti-diagonals (thread t owns row t + 1 and is t steps behind the thread above it, one block barrier
+// per step), the moves are kept as 2-bit codes in shared memory (at most 512 rows x 94 words), and one thread walks
+// the path back and forth as the reference does. Only the times (4 bytes per token) go back to the host.
 //
 // Every operation is an IEEE round-to-nearest intrinsic (no contraction, correctly rounded division and square root),
-// so the cost matrix is bit-identical to the host restatement.
+// so the cost matrix and the times are bit-identical to the host restatement.
 #include "common.cuh"
 #include "launch.h"
 
@@ -113,6 +115,115 @@ __global__ void __launch_bounds__(AL_THREADS) align_cost_kernel(const h16* __res
                 if (r < nr) dst[(size_t)r * TENC] = rh(__fdiv_rn(acc[r], (float)na));
         }
     }
+}
+
+constexpr int DT_THREADS = 512;            // token rows per clip at most
+constexpr int DT_WPR = (TENC + 15) / 16;   // trace words per row: 16 two-bit moves each
+
+__device__ __forceinline__ float pick4(const float4& v, int k) {
+    return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
+// grid (clips), block 512, dynamic shared memory dtw_smem_bytes(mt). cost [clips][mt][1500] f32 as align_cost writes
+// it; times [clips][mt]: entry i < rows[s] the start time of token row i, 0 past them (all 0 when cols[s] = 0).
+__global__ void __launch_bounds__(DT_THREADS, 1) dtw_times_kernel(const float* __restrict__ cost,
+                                                                  const int* __restrict__ rows_of,
+                                                                  const int* __restrict__ cols_of, int mt,
+                                                                  float* __restrict__ times) {
+    extern __shared__ uint32_t tr[];                // [rows][DT_WPR] moves, then the path
+    __shared__ float edge[2][DT_THREADS / 32];      // the last lane's cost per warp, by step parity
+    griddep_wait();  // launched as a programmatic dependent of align_cost_kernel
+    const int s = blockIdx.x, t = threadIdx.x, lane = t & 31, w = t >> 5;
+    const int rows = min(rows_of[s], mt), cols = min(cols_of[s], TENC);
+    float* out = times + (size_t)s * mt;
+    if (rows <= 0 || cols <= 0) {  // align.rs:45-47 (no rows: nothing is timed)
+        for (int i = t; i < mt; i += DT_THREADS) out[i] = 0.f;
+        return;
+    }
+    // align.rs:66-85: cost[i][j] = -x[i-1][j-1] + min(diag, up, left), ties to the later of (diag, up, left);
+    // row 0 is inf past column 0, column 0 inf past row 0, cost[0][0] = 0
+    const bool live = t < rows;
+    const float4* crow = reinterpret_cast<const float4*>(cost + ((size_t)s * mt + t) * TENC);
+    float4 cv = make_float4(0.f, 0.f, 0.f, 0.f), nv = live ? __ldg(crow) : cv;
+    float left = INFINITY, diag = t == 0 ? 0.f : INFINITY, cur = INFINITY;
+    uint32_t bits = 0;
+    const int steps = rows + cols - 1;
+    for (int step = 0; step < steps; step++) {
+        const int j = step - t + 1;  // the column of row t + 1 at this step
+        float up = __shfl_up_sync(0xffffffff, cur, 1);
+        if (lane == 0) up = w > 0 ? edge[(step + 1) & 1][w - 1] : INFINITY;
+        if (live && j >= 1 && j <= cols) {
+            const int k = (j - 1) & 3;
+            if (k == 0) {
+                cv = nv;
+                if (j + 3 < cols) nv = __ldg(crow + ((j - 1) >> 2) + 1);
+            }
+            float c;
+            uint32_t mv;
+            if (diag < up && diag < left) {
+                c = diag;
+                mv = 0;
+            } else if (up < diag && up < left) {
+                c = up;
+                mv = 1;
+            } else {
+                c = left;
+                mv = 2;
+            }
+            // (float)((double)a + (double)b) of two floats is their correctly rounded f32 sum
+            cur = __fadd_rn(-pick4(cv, k), c);
+            left = cur;
+            diag = up;
+            bits |= mv << (2 * ((j - 1) & 15));
+            if (((j - 1) & 15) == 15 || j == cols) {
+                tr[t * DT_WPR + ((j - 1) >> 4)] = bits;
+                bits = 0;
+            }
+        }
+        if (lane == 31) edge[step & 1][w] = cur;
+        __syncthreads();
+    }
+    if (t != 0) return;
+    // align.rs:86-106: the path from (rows, cols) back to (0, 0); row 0 moves left, column 0 moves up
+    short* ptext = reinterpret_cast<short*>(tr + rows * DT_WPR);
+    short* ptime = ptext + rows + cols;
+    int i = rows, j = cols, n = 0;
+    while (i > 0 || j > 0) {
+        ptext[n] = (short)(i - 1);
+        ptime[n] = (short)(j - 1);
+        n++;
+        const uint32_t mv = i == 0 ? 2u : j == 0 ? 1u : (tr[(i - 1) * DT_WPR + ((j - 1) >> 4)] >> (2 * ((j - 1) & 15))) & 3u;
+        if (mv == 0) {
+            i--;
+            j--;
+        } else if (mv == 1) {
+            i--;
+        } else {
+            j--;
+        }
+    }
+    // align.rs:48-62, in the path's forward order (index n - 1 first): a row's time is that of its first entry
+    int k_out = 0;
+    for (int k = n - 1; k >= 0 && k_out < rows; k--)
+        if (k == n - 1 || ptext[k] != ptext[k + 1]) out[k_out++] = __double2float_rn((double)ptime[k] * 0.02);
+    const float last = k_out > 0 ? out[k_out - 1] : 0.f;
+    for (; k_out < mt; k_out++) out[k_out] = k_out < rows ? last : 0.f;
+}
+
+static size_t dtw_smem_bytes(int mt) { return (size_t)mt * DT_WPR * 4 + (size_t)(mt + TENC) * 2 * 2; }
+
+int launch_dtw_times(const void* cost, const int* rows, const int* cols, int n, int mt, void* times, cudaStream_t st) {
+    if (n < 1 || mt < 1 || mt > DT_THREADS) return fail("dtw_times: bad shape (1 <= max_t <= 512)");
+    if ((uintptr_t)cost & 15) return fail("dtw_times: cost must be 16-byte aligned");
+    DevCtx& dc = dev_ctx();
+    if (!dc.ok) return fail(dc.err);
+    return check_pdl(launch_pdl(dtw_times_kernel, dim3(n), dim3(DT_THREADS), dtw_smem_bytes(mt), st,
+                                (const float*)cost, rows, cols, mt, (float*)times),
+                     "dtw_times");
+}
+
+void init_align_attrs() {
+    cudaFuncSetAttribute(dtw_times_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dtw_smem_bytes(DT_THREADS));
 }
 
 int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,

@@ -105,6 +105,10 @@ int mmz_align_cost(const void* align, const int* rows, const int* cols, int n, i
     return launch_align_cost(align, rows, cols, n, np, max_t, na, cost, S(stream));
 }
 
+int mmz_dtw_times(const void* cost, const int* rows, const int* cols, int n, int max_t, void* times, void* stream) {
+    return launch_dtw_times(cost, rows, cols, n, max_t, times, S(stream));
+}
+
 int mmz_times_from_cost(const float* cost, int rows, int cols, int ld, float* out) {
     if (rows < 1 || cols < 0 || ld < cols) return fail("times_from_cost: bad shape (cols <= ld)");
     times_from_cost(cost, rows, cols, ld, out);

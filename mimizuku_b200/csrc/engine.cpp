@@ -403,7 +403,8 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
     if (k_->native()) {
         cost_ = (float*)alloc(b * mt * TENC_ * 4);
         rc_ = (int*)alloc(b * 2 * 4);
-        if (!cost_ || !rc_) {
+        tms_ = (float*)alloc(b * mt * 4);
+        if (!cost_ || !rc_ || !tms_) {
             err_ = "device memory allocation failed";
             return;
         }
@@ -729,7 +730,7 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
     threads = std::min(threads, n);
     d2h_bytes_ = (size_t)n * mt * 4;
     if (k_->native()) {
-        // the DTW cost of every clip on the GPU (align.rs:6-43), then only 4 bytes per (row, frame) to the host
+        // the DTW cost and the DTW itself for every clip on the GPU (align.rs:6-106): only the times come back
         std::vector<int> rc(2 * (size_t)n);
         for (int s = 0; s < n; s++) {
             rc[s] = nrows[s];
@@ -737,31 +738,21 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
         }
         CUDA_CK(cudaMemcpyAsync(rc_, rc.data(), rc.size() * 4, cudaMemcpyHostToDevice, st_));
         CK(launch_align_cost(align_, rc_, rc_ + n, n, np, mt, na, cost_, st_));
-        k_->launches++;
-        std::vector<float> ch((size_t)n * mt * TENC_);
-        for (int s = 0; s < n; s++)
-            if (nrows[s] > 0) {
-                const size_t off = (size_t)s * mt * TENC_;
-                CUDA_CK(cudaMemcpyAsync(ch.data() + off, cost_ + off, (size_t)nrows[s] * TENC_ * 4,
-                                        cudaMemcpyDeviceToHost, st_));
-                d2h_bytes_ += (size_t)nrows[s] * TENC_ * 4;
-            }
+        CK(launch_dtw_times(cost_, rc_, rc_ + n, n, mt, tms_, st_));
+        k_->launches += 2;
+        std::vector<float> th((size_t)n * mt);
+        CUDA_CK(cudaMemcpyAsync(th.data(), tms_, th.size() * 4, cudaMemcpyDeviceToHost, st_));
+        d2h_bytes_ += th.size() * 4;
         CUDA_CK(cudaStreamSynchronize(st_));
-        auto work = [&](int w) {
-            for (int s = w; s < n; s += threads) {
-                float* ts = times + (size_t)s * mt;
-                std::fill(ts, ts + mt, 0.f);
-                lens[s] = nseq[s];
-                const int rows = nrows[s];
-                if (rows <= 0) continue;
-                times_from_cost(ch.data() + (size_t)s * mt * TENC_, rows, frames[s] / 2, TENC_, ts + np);
-                ts[nseq[s] - 1] = ts[np + rows - 1];
-            }
-        };
-        std::vector<std::thread> th;
-        for (int w = 1; w < threads; w++) th.emplace_back(work, w);
-        work(0);
-        for (auto& t : th) t.join();
+        for (int s = 0; s < n; s++) {
+            float* ts = times + (size_t)s * mt;
+            std::fill(ts, ts + mt, 0.f);
+            lens[s] = nseq[s];
+            const int rows = nrows[s];
+            if (rows <= 0) continue;
+            std::copy(th.data() + (size_t)s * mt, th.data() + (size_t)s * mt + rows, ts + np);
+            ts[nseq[s] - 1] = ts[np + rows - 1];
+        }
     } else {
         // the reference's path: every recorded probability to the host, jump_times per clip there (align.rs:8-63)
         std::vector<uint16_t> a16(total);

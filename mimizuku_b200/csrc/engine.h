@@ -126,6 +126,7 @@ class Engine {
     void *xkv_buf_, *x_, *hb_, *att_, *dout_, *dbias_, *logits_, *kc_, *vc_, *s_, *stat_, *part_, *align_;
     float* cost_ = nullptr;  // native image: the token-timestamp DTW cost [bmax][max_t][1500], reduced on the GPU
     int* rc_ = nullptr;      // native image: token rows and frame columns per clip for the cost kernel
+    float* tms_ = nullptr;   // native image: the token start times [bmax][max_t] from the GPU DTW
     size_t d2h_bytes_ = 0;   // bytes the last transcribe copied device -> host
     int *tok_, *done_, *ctr_, *aslot_;
     unsigned char *sup_;

@@ -56,6 +56,7 @@ void init_dec_attn_attrs(DevCtx& c);
 int launch_wait_selftest(int limit_ms, cudaStream_t st);
 void init_enc_attn_attrs();
 void init_dec_linear_attrs();
+void init_align_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
 size_t cross_attn_scratch_bytes(int batch, int d);
@@ -79,6 +80,7 @@ int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, v
 // the DTW cost of the token timestamps for a batch of clips (align.cu)
 int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,
                       cudaStream_t st);
+int launch_dtw_times(const void* cost, const int* rows, const int* cols, int n, int mt, void* times, cudaStream_t st);
 
 // engine-side elementwise and token kernels (misc.cu)
 int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,

@@ -78,6 +78,7 @@ DevCtx& dev_ctx() {
     init_dec_attn_attrs(c);
     init_enc_attn_attrs();
     init_dec_linear_attrs();
+    init_align_attrs();
     cudaGetLastError();
     c.ok = true;
     c.err = "";
