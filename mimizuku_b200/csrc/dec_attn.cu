@@ -268,16 +268,17 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
 }
 
 // grid (8, heads, B), block 128; launched as a programmatic dependent of cross_scores_kernel
-__global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict__ kv, XScratch xs,
+__global__ void __launch_bounds__(128, 8) cross_pv_kernel(const h16* __restrict__ kv, XScratch xs,
                                                           h16* __restrict__ align, const int* __restrict__ aslot,
                                                           const int* __restrict__ ctr, const int* __restrict__ done,
                                                           int layer, int nl, int d, int na, int maxT, unsigned* status,
                                                           unsigned long long limit_ns) {
-    __shared__ __align__(128) h16 vs[XPER * HD];  // this CTA's V slice, bulk copies issued before the wait
+    __shared__ __align__(128) h16 vs[XPER * HD];  // this CTA's V slice (bulk copies issued before the wait), then
+                                                  // the group partials
     __shared__ float p[XPER];
     __shared__ float2 gs[XNCH];
-    __shared__ float red[XCPC][16][HD];
     __shared__ uint64_t bar[XCPC];
+    static_assert(XCPC * 16 * HD * 4 <= XPER * HD * 2, "the group partials fit in the V slice");
     __shared__ int abort;
     griddep_launch_dependents();  // the combine kernel may be scheduled as soon as every CTA here is resident
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
@@ -317,11 +318,14 @@ __global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict_
     }
     __syncthreads();
     // P.V per chunk: 16 groups x 8 lanes, a lane owns 8 of the 64 columns (kernels/whisper.cu:421-438); the three
-    // chunks' group sums meet in shared memory behind one barrier
+    // chunks' group sums then meet in the V slice's space (keeping shared memory at 26 KB: 8 CTAs per SM)
+    float a[XCPC][8];
+#pragma unroll
     for (int c = 0; c < XCPC; c++) {
         mbar_wait(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 4 + c);
         const int nc = min(XCH, n - c * XCH);
-        float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 8; e++) a[c][e] = 0.f;
         for (int jj = grp; jj < nc; jj += 16) {
             const uint4 u = *reinterpret_cast<const uint4*>(vs + (c * XCH + jj) * HD + sub * 8);
             const __half2* p2 = reinterpret_cast<const __half2*>(&u);
@@ -329,18 +333,22 @@ __global__ void __launch_bounds__(128, 6) cross_pv_kernel(const h16* __restrict_
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 float2 v = __half22float2(p2[e]);
-                a[2 * e] += pj * v.x;
-                a[2 * e + 1] += pj * v.y;
+                a[c][2 * e] += pj * v.x;
+                a[c][2 * e + 1] += pj * v.y;
             }
         }
-#pragma unroll
-        for (int e = 0; e < 8; e++) red[c][grp][sub * 8 + e] = a[e];
     }
+    __syncthreads();  // V is no longer read
+    float* red = reinterpret_cast<float*>(vs);  // [XCPC][16][HD]
+#pragma unroll
+    for (int c = 0; c < XCPC; c++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) red[(c * 16 + grp) * HD + sub * 8 + e] = a[c][e];
     __syncthreads();
     for (int i = t; i < XCPC * HD; i += 128) {
         const int c = i / HD, col = i % HD;
         float acc = 0.f;
-        for (int g = 0; g < 16; g++) acc += red[c][g][col];
+        for (int g = 0; g < 16; g++) acc += red[(c * 16 + g) * HD + col];
         xs.part[((long)bh * XNCH + r * XCPC + c) * HD + col] = acc;
     }
     if (t == 0 && abort)
