@@ -94,11 +94,11 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             mbar_init(&s.bar_ve[i], 1);
         }
         mbar_init(&s.bar_sf, 1);
-        mbar_init(&s.bar_sfree, 256);
-        mbar_init(&s.bar_pf, 256);
+        mbar_init(&s.bar_sfree, 8);  // one arrival per softmax warp
+        mbar_init(&s.bar_pf, 8);
         mbar_init(&s.bar_od, 1);
         mbar_init(&s.bar_fin, 1);
-        for (int i = 0; i < 4; i++) mbar_init(&s.bar_x[i], 64);
+        for (int i = 0; i < 4; i++) mbar_init(&s.bar_x[i], 2);  // the two warps of a lane quarter
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -205,7 +205,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             uint32_t raw[64];
             tmem_ld64(tSh, raw);
             tc_fence_before();
-            mbar_arrive(&s.bar_sfree);  // this thread's scores are in registers: the next QK product may start
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.bar_sfree);  // the warp's scores are in registers: the next QK may start
             float* sv = reinterpret_cast<float*>(raw);
             if (last) {
 #pragma unroll
@@ -223,7 +224,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             float tmax = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
             // exchange with the partner thread of this row (the other key half)
             s.xmax[j & 1][hf][row] = tmax;
-            mbar_arrive(&s.bar_x[quarter]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.bar_x[quarter]);
             ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_x[quarter], j & 1, abort, limit_ns, status, K_ENC, 33));
             if (!ok) break;
             tmax = fmaxf(tmax, s.xmax[j & 1][hf ^ 1][row]) * sl2;
@@ -273,13 +275,15 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&s.bar_pf);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.bar_pf);
         }
         if (ok) ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_od, (NKT - 1) & 1, abort, limit_ns, status, K_ENC, 32));
         if (ok) {
             // the row sum is the two halves' shares
             s.xmax[NKT & 1][hf][row] = l;
-            mbar_arrive(&s.bar_x[quarter]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s.bar_x[quarter]);
             ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_x[quarter], NKT & 1, abort, limit_ns, status, K_ENC, 34));
         }
         if (ok) {
