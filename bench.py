@@ -124,7 +124,8 @@ def cpu_baseline(threads):
 
 
 def kernel_rooflines(e, cfg, torch, impl):
-    """Live CUDA-event timings of the hot kernels on the engine's stream and buffers (inputs larger than L2):
+    """Live CUDA-event timings of the hot kernels, replayed from a CUDA graph on the engine's stream and buffers
+    (inputs larger than L2):
     cross-attention (the dominant kernel of the decoding step), self-attention at the mean context, and encoder
     attention. impl "reference" times the reference's kernels (cross_scores + cross_pv + cross_combine, kv_write +
     self_attn, enc_flash) with src/model.rs's launch geometry on the same buffers."""
@@ -147,14 +148,23 @@ def kernel_rooflines(e, cfg, torch, impl):
     oute = torch.empty(g, 1500, d, device="cuda", dtype=torch.float16)
 
     def timed(fn, iters):
+        """device time per call of `iters` consecutive calls captured in one CUDA graph (no host launch cost in
+        the timed replay, as in the decoding step's own graph)"""
         with torch.cuda.stream(st):
             for i in range(3):
                 fn(i)
-            a.record(st)
+        st.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
             for i in range(iters):
                 fn(i)
+        with torch.cuda.stream(st):
+            gr.replay()
+            a.record(st)
+            gr.replay()
             b.record(st)
         b.synchronize()
+        del gr
         return a.elapsed_time(b) * 1e-3 / iters
 
     if impl == "native":

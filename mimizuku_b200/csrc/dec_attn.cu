@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(128)
         const int st = i % SSTAGE;
         const bool is_k = i < ntile;
         const int j0 = (is_k ? i : i - ntile) * STILE;
-        mbar_wait(&s.full[st], (i / SSTAGE) & 1, &s.abort, limit_ns, status, K_SELF, 1);
+        mbar_wait_spin(&s.full[st], (i / SSTAGE) & 1, &s.abort, limit_ns, status, K_SELF, 1);
         h16* tile = s.ring[st];
         if (p >= j0 && p < j0 + STILE) {  // the current position comes from qkv (its cache row is written above)
             if (t < 8) row_copy8(tile + (p - j0) * HD, qkv + qrow + (is_k ? d : 2 * d) + hh * HD, t);
@@ -322,7 +322,7 @@ __global__ void __launch_bounds__(128, 8) cross_pv_kernel(const h16* __restrict_
     float a[XCPC][8];
 #pragma unroll
     for (int c = 0; c < XCPC; c++) {
-        mbar_wait(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 4 + c);
+        mbar_wait_spin(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 4 + c);
         const int nc = min(XCH, n - c * XCH);
 #pragma unroll
         for (int e = 0; e < 8; e++) a[c][e] = 0.f;
