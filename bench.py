@@ -88,10 +88,38 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_features(n_mels, first_clip, count):
+def make_features(n_mels, first_clip, count, threads):
+    """The benchmark's seeded clips and their log-mel features on the host (src/audio.rs's restatement on `threads`
+    host threads, as src/transcribe.rs:25-56); also returns the clips and the host time."""
     import mimizuku_b200 as m
     ys = [m.synth_clip(1000003 * (first_clip + i) + 17) for i in range(count)]
-    return m.log_mel_batch(ys, n_mels)
+    t0 = time.perf_counter()
+    mel, frames = m.log_mel_batch(ys, n_mels, threads=threads)
+    return mel, frames, ys, time.perf_counter() - t0
+
+
+def features_gpu(ys, n_mels, torch):
+    """The same features on the GPU from pinned host audio: host-to-device copy of the samples, then the DFT,
+    filterbank and log kernels; seconds for the batch (one warm-up call first, which uploads the tables)."""
+    import mimizuku_b200 as m
+    count = len(ys)
+    audio = torch.zeros((count, 480000), dtype=torch.float32).pin_memory()
+    for i, y in enumerate(ys):
+        audio[i, :len(y)] = torch.from_numpy(y[:480000])
+    lens = torch.tensor([min(len(y), 480000) for y in ys], dtype=torch.int32, device="cuda")
+    dev = torch.empty((count, 480000), dtype=torch.float32, device="cuda")
+    out = torch.empty((count, n_mels, 3000), dtype=torch.float32, device="cuda")
+    work = torch.empty(m.log_mel_gpu_work_bytes(count), dtype=torch.uint8, device="cuda")
+    best = None
+    for _ in range(3):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        dev.copy_(audio, non_blocking=True)
+        m.log_mel_gpu(dev, lens, n_mels, out, work=work, stream=torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        t = time.perf_counter() - t0
+        best = t if best is None else min(best, t)
+    return best, audio.numel() * 4
 
 
 def cpu_baseline(threads):
@@ -248,7 +276,7 @@ def main():
     hbm_peak, tc_peak, peak_src = peaks()
     n_threads = args.threads or max(1, (os.cpu_count() or 8) // max(1, world))
 
-    mel, frames = make_features(cfg.n_mels, rank * CLIPS_PER_GPU, CLIPS_PER_GPU)
+    mel, frames, clips, t_feat_host = make_features(cfg.n_mels, rank * CLIPS_PER_GPU, CLIPS_PER_GPU, n_threads)
     kimg = REF_FATBIN if args.impl == "reference" else None
     e = m.Engine(cfg, bmax=CLIPS_PER_GPU, eg=8, device=local, kernel_image=kimg, seed=1234,
                  suppress=[cfg.eos])
@@ -373,6 +401,12 @@ def main():
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
     }
+    if args.impl == "native":  # log-mel is outside the clips/s metric (features are reported separately)
+        t_feat_gpu, feat_h2d = features_gpu(clips, cfg.n_mels, torch)
+        line["features"] = {"clips": CLIPS_PER_GPU, "host_s": round(t_feat_host, 4), "host_threads": n_threads,
+                            "gpu_s": round(t_feat_gpu, 5), "gpu_h2d_bytes": int(feat_h2d),
+                            "what": "log-mel of 30 s clips (src/audio.rs): host restatement vs the GPU kernels "
+                                    "(host-to-device copy of the samples included)"}
     if args.impl == "reference":
         line["impl"] = "reference"
         line["reference_kind"] = ("the reference's own kernels (kernels/whisper.cu, compute_80 PTX JIT-compiled on "

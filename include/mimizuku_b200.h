@@ -132,6 +132,15 @@ int mmz_dtw(const double* m, int rows, int cols, int* text, int* time, int* len)
  * src/audio.rs:192-237. */
 int mmz_log_mel(const float* y, long n, int n_mels, float* out, int* frames);
 /* The same for `count` clips on `threads` host threads (src/transcribe.rs:25-56); out [count][n_mels][3000]. */
+/* The same features for a batch on the GPU: audio [count][480000] f32 device (each clip's first 30 s; samples past
+ * lens[s] are ignored), lens [count] int32 device (samples that hold audio), out [count][n_mels][3000] f32 device;
+ * work: mmz_log_mel_gpu_work_bytes(count) device bytes, 16-byte aligned. The DFT runs in f64 with the host's summation
+ * order and roundings, so the power spectra equal mmz_log_mel_batch's bit for bit; log10 is taken in f64 and rounded.
+ * The first call per (device, n_mels) uploads the host's filterbank tables (1.4 MB, synchronously); later calls are
+ * asynchronous on `stream`. The frame counts are the host's: min((lens[s] + 159) / 160, 3000). */
+size_t mmz_log_mel_gpu_work_bytes(int count);
+int mmz_log_mel_gpu(const float* audio, const int* lens, int count, int n_mels, float* out, void* work,
+                    size_t work_bytes, void* stream);
 int mmz_log_mel_batch(const float* const* ys, const long* ns, int count, int n_mels, int threads, float* out,
                       int* frames);
 /* A seeded synthetic 30 s clip: 1-8 sinusoids in 80-4000 Hz plus Gaussian noise at 10 dB SNR. */

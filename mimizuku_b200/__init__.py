@@ -68,6 +68,8 @@ SIGNATURES = {
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
     "mmz_log_mel": (_I, [_FP, _L, _I, _FP, _IP]),
+    "mmz_log_mel_gpu_work_bytes": (_ULL, [_I]),
+    "mmz_log_mel_gpu": (_I, [_P, _P, _I, _I, _P, _P, _ULL, _P]),
     "mmz_log_mel_batch": (_I, [ctypes.POINTER(_FP), ctypes.POINTER(_L), _I, _I, _I, _FP, _IP]),
     "mmz_synth_clip": (_I, [_ULL, _FP, _L]),
     "mmz_engine_create": (_P, [ctypes.POINTER(mmz_dims), ctypes.POINTER(mmz_gencfg), _I, _I, _I, ctypes.c_char_p,
@@ -294,6 +296,24 @@ def log_mel_batch(clips, n_mels, threads=0):
     _check(lib.mmz_log_mel_batch(ptrs, lens, n, n_mels, threads, _fp(out), frames.ctypes.data_as(_IP)),
            "log_mel_batch")
     return out, frames
+
+
+def log_mel_gpu_work_bytes(count):
+    """Bytes of device work space log_mel_gpu needs for `count` clips."""
+    return lib.mmz_log_mel_gpu_work_bytes(count)
+
+
+def log_mel_gpu(audio, lens, n_mels, out, work=None, stream=None):
+    """src/audio.rs:192-237 on the GPU for a batch: audio float32 device [count][480000], lens int32 device [count]
+    (samples that hold audio) -> out float32 device [count][n_mels][3000]. work: a device buffer of at least
+    log_mel_gpu_work_bytes(count) bytes (allocated here when None)."""
+    count = lens.shape[0]
+    if work is None:
+        import torch
+        work = torch.empty(log_mel_gpu_work_bytes(count), dtype=torch.uint8, device=out.device)
+    nbytes = work.numel() * work.element_size()
+    _check(lib.mmz_log_mel_gpu(_ptr(audio), _ptr(lens), count, n_mels, _ptr(out), _ptr(work), nbytes,
+                               _stream(stream)), "log_mel_gpu")
 
 
 def synth_clip(seed, n=480000):

@@ -136,6 +136,13 @@ int mmz_log_mel_batch(const float* const* ys, const long* ns, int count, int n_m
     return 0;
 }
 
+size_t mmz_log_mel_gpu_work_bytes(int count) { return count < 1 ? 0 : log_mel_work_bytes(count); }
+
+int mmz_log_mel_gpu(const float* audio, const int* lens, int count, int n_mels, float* out, void* work,
+                    size_t work_bytes, void* stream) {
+    return launch_log_mel(audio, lens, count, n_mels, out, work, work_bytes, S(stream));
+}
+
 int mmz_synth_clip(unsigned long long seed, float* y, long n) {
     if (n < 0) return fail("synth_clip: bad length");
     synth_clip(seed, y, n);

@@ -81,6 +81,9 @@ int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, v
 int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,
                       cudaStream_t st);
 int launch_dtw_times(const void* cost, const int* rows, const int* cols, int n, int mt, void* times, cudaStream_t st);
+size_t log_mel_work_bytes(int count);
+int launch_log_mel(const float* audio, const int* lens, int count, int n_mels, float* out, void* work,
+                   size_t work_bytes, cudaStream_t st);
 
 // engine-side elementwise and token kernels (misc.cu)
 int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe, void* x, int batch, int maxT, int d,
