@@ -67,7 +67,7 @@ def build(force=False, jobs=None, verbose=False):
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
         cmd = [NVCC] + ARCH + ["-shared", "-o", tmp] + objs + [
-            f"-L{CUDA}/lib64", "-lcublas", "-Xlinker", f"-rpath,{CUDA}/lib64", "-cudart", "static"]
+            f"-L{CUDA}/lib64", "-lcublas", "-lcublasLt", "-Xlinker", f"-rpath,{CUDA}/lib64", "-cudart", "static"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{' '.join(cmd)}\n{r.stdout}{r.stderr}")

@@ -358,6 +358,10 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         return;
     }
     ws_ = alloc(WS_BYTES);
+    if (k_->native() && cublasLtCreate(&lt_) != CUBLAS_STATUS_SUCCESS) {
+        err_ = "cuBLASLt setup failed";
+        return;
+    }
     if (!ws_ || cublasSetWorkspace(blas_, ws_, WS_BYTES) != CUBLAS_STATUS_SUCCESS) {
         err_ = "cuBLAS workspace";
         return;
@@ -455,6 +459,7 @@ Engine::~Engine() {
     k_.reset();
     for (void* p : allocs_) cudaFree(p);
     if (blas_) cublasDestroy(blas_);
+    if (lt_) cublasLtDestroy(lt_);
     if (st_) cudaStreamDestroy(st_);
 }
 
@@ -543,6 +548,79 @@ int Engine::lin_onto_bias(const void* x, int ldx, const Lin& l, void* y, int ldy
     return matmul(true, false, n, m, k, 1.f, l.w, k, 0, x, ldx, 0, 1.f, y, ldy, 0, 1);
 }
 
+// The native encoder's linear layers take their bias in the GEMM's epilogue instead of a bias image that the GEMM
+// reads back (model.rs:543-623 writes the image, then accumulates onto it): one write of y instead of two writes and a
+// read. The fp32 accumulator plus the bias is rounded once either way; the algorithm is cuBLASLt's first heuristic
+// choice for the shape, so the sums may associate differently from cublasGemmEx's (the encoder is compared with the
+// reference's within tolerance, not bit for bit).
+int Engine::gemm_bias(const void* x, int ldx, const void* w, long long sw, const void* bias, void* y, int ldy,
+                      long long sy, int m, int n, int k, int batch) {
+    if (!lt_) return -2;
+    const long long key[8] = {m, n, k, batch, ldx, ldy, sw, sy};
+    cublasLtMatmulDesc_t op = nullptr;
+    cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+    int rc = -2;
+    const cublasOperation_t tA = CUBLAS_OP_T, tB = CUBLAS_OP_N;
+    const cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_BIAS;
+    const cudaDataType_t bt = CUDA_R_16F;
+    const long long bstride = n, zero = 0;
+    const float one = 1.f, nil = 0.f;
+    auto ok = [](cublasStatus_t s) { return s == CUBLAS_STATUS_SUCCESS; };
+    if (ok(cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F)) &&
+        ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &tA, sizeof(tA))) &&
+        ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tB, sizeof(tB))) &&
+        ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof(epi))) &&
+        ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof(bias))) &&
+        ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bt, sizeof(bt))) &&
+        (batch == 1 || ok(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_BATCH_STRIDE, &bstride,
+                                                          sizeof(bstride)))) &&
+        // column-major: W^T (n x k, stored k x n), x^T (k x m), y^T (n x m)
+        ok(cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, k, n, k)) && ok(cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, k, m, ldx)) &&
+        ok(cublasLtMatrixLayoutCreate(&lc, CUDA_R_16F, n, m, ldy))) {
+        bool lay = true;
+        if (batch > 1)
+            for (auto [l, s] : {std::pair<cublasLtMatrixLayout_t, long long>{la, sw}, {lb, zero}, {lc, sy}}) {
+                lay = lay && ok(cublasLtMatrixLayoutSetAttribute(l, CUBLASLT_MATRIX_LAYOUT_BATCH_COUNT, &batch,
+                                                                 sizeof(batch))) &&
+                      ok(cublasLtMatrixLayoutSetAttribute(l, CUBLASLT_MATRIX_LAYOUT_STRIDED_BATCH_OFFSET, &s,
+                                                          sizeof(s)));
+            }
+        LtPlan* plan = nullptr;
+        for (LtPlan& p : lt_plans_)
+            if (std::equal(key, key + 8, p.key)) plan = &p;
+        if (lay && !plan) {
+            LtPlan p{};
+            std::copy(key, key + 8, p.key);
+            cublasLtMatmulPreference_t pref = nullptr;
+            const size_t wsb = WS_BYTES;
+            cublasLtMatmulHeuristicResult_t res{};
+            int nres = 0;
+            p.ok = ok(cublasLtMatmulPreferenceCreate(&pref)) &&
+                   ok(cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &wsb,
+                                                           sizeof(wsb))) &&
+                   ok(cublasLtMatmulAlgoGetHeuristic(lt_, op, la, lb, lc, lc, pref, 1, &res, &nres)) && nres > 0;
+            if (pref) cublasLtMatmulPreferenceDestroy(pref);
+            p.algo = res.algo;
+            lt_plans_.push_back(p);
+            plan = &lt_plans_.back();
+        }
+        if (lay && plan && plan->ok)
+            rc = ok(cublasLtMatmul(lt_, op, &one, w, la, x, lb, &nil, y, lc, y, lc, &plan->algo, ws_, WS_BYTES, st_))
+                     ? 0
+                     : failf("cublasLtMatmul failed");
+    }
+    if (la) cublasLtMatrixLayoutDestroy(la);
+    if (lb) cublasLtMatrixLayoutDestroy(lb);
+    if (lc) cublasLtMatrixLayoutDestroy(lc);
+    if (op) cublasLtMatmulDescDestroy(op);
+    return rc;
+}
+
+int Engine::lin_enc(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k) {
+    const int r = gemm_bias(x, ldx, l.w, 0, l.b, y, ldy, 0, m, n, k, 1);
+    return r == -2 ? lin(x, ldx, l, y, ldy, m, n, k) : r;
+}
+
 // model.rs:543-625
 int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     if (gn < 1 || gn > eg_ || slot0 < 0 || slot0 + gn > bmax_) return fail("encode: bad group");
@@ -550,22 +628,22 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     const long r1 = (long)gn * NFRAMES, r2 = (long)gn * TENC_;
     if (mel16 != mel_) CUDA_CK(cudaMemcpyAsync(mel_, mel16, (size_t)gn * nm * NFRAMES * 2, cudaMemcpyDeviceToDevice, st_));
     CK(k_->im2col1(mel_, x1_, r1 * 3 * nm, nm, st_));
-    CK(lin(x1_, 3 * nm, conv1_, h1_, d, r1, d, 3 * nm));
+    CK(lin_enc(x1_, 3 * nm, conv1_, h1_, d, r1, d, 3 * nm));
     CK(k_->gelu(h1_, r1 * d, st_));
     CK(k_->im2col2(h1_, x2_, r2 * 3 * d, d, st_));
-    CK(lin(x2_, 3 * d, conv2_, ex_, d, r2, d, 3 * d));
+    CK(lin_enc(x2_, 3 * d, conv2_, ex_, d, r2, d, 3 * d));
     CK(k_->gelu(ex_, r2 * d, st_));
     CK(k_->add_pos(ex_, epos_, r2, d, TENC_, st_));
     CK(k_->layernorm(ex_, enc_[0].ln1, eh_, r2, d, st_));
     for (size_t i = 0; i < enc_.size(); i++) {
         const EncLayer& l = enc_[i];
-        CK(lin(eh_, d, l.qkv, eqkv_, 3 * d, r2, 3 * d, d));
+        CK(lin_enc(eh_, d, l.qkv, eqkv_, 3 * d, r2, 3 * d, d));
         CK(k_->enc_attn(eqkv_, eatt_, gn, d, nh, st_));
-        CK(lin(eatt_, d, l.o, eh_, d, r2, d, d));
+        CK(lin_enc(eatt_, d, l.o, eh_, d, r2, d, d));
         CK(k_->add_layernorm(ex_, eh_, l.ln2, eh_, r2, d, st_));
-        CK(lin(eh_, d, l.fc1, ef_, ff, r2, ff, d));
+        CK(lin_enc(eh_, d, l.fc1, ef_, ff, r2, ff, d));
         CK(k_->gelu(ef_, r2 * ff, st_));
-        CK(lin(ef_, ff, l.fc2, eh_, d, r2, d, ff));
+        CK(lin_enc(ef_, ff, l.fc2, eh_, d, r2, d, ff));
         const Ln& next = i + 1 < enc_.size() ? enc_[i + 1].ln1 : eln_;
         CK(k_->add_layernorm(ex_, eh_, next, eh_, r2, d, st_));
     }
@@ -574,9 +652,14 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     const int nblk = nl * 2 * nh;
     for (int c = 0; c < gn; c++) {
         void* dst = (char*)xkv_buf_ + 2 * (size_t)(slot0 + c) * xkv;
+        const void* xc = (char*)eh_ + 2 * (size_t)c * TENC_ * d;
+        const int r = gemm_bias(xc, d, xkv_.w, (long long)HDIM * d, xkv_.b, dst, HDIM, (long long)TENC_ * HDIM, TENC_,
+                                HDIM, d, nblk);
+        if (r == 0) continue;
+        if (r != -2) return r;
         CK(k_->fill_bias_heads(dst, xkv_.b, xkv / 8, st_));
-        CK(matmul(true, false, HDIM, TENC_, d, 1.f, xkv_.w, d, (long long)HDIM * d, (char*)eh_ + 2 * (size_t)c * TENC_ * d,
-                  d, 0, 1.f, dst, HDIM, (long long)TENC_ * HDIM, nblk));
+        CK(matmul(true, false, HDIM, TENC_, d, 1.f, xkv_.w, d, (long long)HDIM * d, xc, d, 0, 1.f, dst, HDIM,
+                  (long long)TENC_ * HDIM, nblk));
     }
     return 0;
 }

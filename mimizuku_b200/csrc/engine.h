@@ -8,6 +8,7 @@
 //   fatbin     any image that exports the reference's 23 kernel names with its argument lists (the reference's own
 //              kernels/whisper.cu build is one), launched by name with the reference's grid geometry (model.rs)
 #pragma once
+#include <cublasLt.h>
 #include <cublas_v2.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -81,6 +82,11 @@ class Engine {
    private:
     int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
     int lin_onto_bias(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
+    // native image, encoder: y = x W^T + bias with the bias added in the GEMM's epilogue (cuBLASLt), batched over
+    // `batch` weight blocks (strides sw, sy; the bias advances by n per block); -2 when no algorithm supports it
+    int gemm_bias(const void* x, int ldx, const void* w, long long sw, const void* bias, void* y, int ldy,
+                  long long sy, int m, int n, int k, int batch);
+    int lin_enc(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
     int matmul(bool ta, bool tb, int m, int n, int k, float alpha, const void* a, int lda, long long sa, const void* b,
                int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch);
     void* alloc(size_t bytes);
@@ -94,6 +100,13 @@ class Engine {
     int dev_ = 0;
     cudaStream_t st_ = nullptr;
     cublasHandle_t blas_ = nullptr;
+    cublasLtHandle_t lt_ = nullptr;
+    struct LtPlan {
+        long long key[8];
+        cublasLtMatmulAlgo_t algo;
+        bool ok;
+    };
+    std::vector<LtPlan> lt_plans_;  // heuristic choice per encoder GEMM shape
     std::unique_ptr<Kernels> k_;
     std::vector<void*> allocs_;
     size_t allocated_ = 0;
