@@ -4,6 +4,9 @@
     python -m mimizuku_b200.profile_kernels enc            encoder attention, large-v3, 8 clips x 20 heads
     python -m mimizuku_b200.profile_kernels cross          cross-attention, large-v3, batch 32, one layer
     python -m mimizuku_b200.profile_kernels self [p]       self-attention, large-v3, batch 32, position p (default 223)
+    python -m mimizuku_b200.profile_kernels step [n]       n decoding steps (default 4) of the large-v3 engine at batch
+                                                           32 from one captured graph, inside the NVTX range "steps"
+                                                           (ncu --nvtx --nvtx-include "steps/" captures only those)
 """
 import sys
 
@@ -46,6 +49,25 @@ def main(argv):
         ctr = torch.tensor([p, 0, 0, 0], dtype=torch.int32, device="cuda")
         for _ in range(4):
             m.self_attn(qkv, kc, vc, out, ctr, done, mt, d)
+    elif which == "step":
+        import numpy as np
+        n = int(argv[1]) if len(argv) > 1 else 4
+        cfg = m.LARGE_V3
+        e = m.Engine(cfg, bmax=32, eg=8, device=0, seed=1234, suppress=[cfg.eos])
+        mel16 = torch.randn(32, cfg.n_mels, 3000, device="cuda").half()
+        for g0 in range(0, 32, 8):
+            e.encode(mel16[g0].data_ptr(), 8, g0)
+        e.reset(np.tile(np.array(cfg.prompt, np.int32), (32, 1)))
+        e.capture(32, len(cfg.prompt))
+        for _ in range(len(cfg.prompt) + 8):  # past the prompt, graph captured and warm
+            e.replay()
+        e.sync()
+        torch.cuda.nvtx.range_push("steps")
+        for _ in range(n):
+            e.replay()
+        e.sync()
+        torch.cuda.nvtx.range_pop()
+        e.close()
     else:
         raise SystemExit(__doc__)
     torch.cuda.synchronize()
