@@ -387,7 +387,7 @@ def main():
         "e2e": {"value": round(e2e, 3), "unit": "clips/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
                 "stage_s_per_step": [round(x / args.steps, 4) for x in stages]},
-        "roofline": {"kernel": ("cross_scores_kernel+cross_pv_kernel" if args.impl == "native"
+        "roofline": {"kernel": ("cross_scores_kernel+cross_pv_kernel+cross_combine_kernel" if args.impl == "native"
                                 else "cross_scores+cross_pv+cross_combine"),
                      "bound": "hbm", "achieved": round(bx / tx / 1e9, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(bx / tx / 1e9 / hbm_peak, 3), "traffic": traffic,
