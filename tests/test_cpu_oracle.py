@@ -142,6 +142,50 @@ def test_log_mel_tone_peaks_near_its_frequency():
     assert np.all(mel[:, 250:] == mel.min())  # frames past the audio sit at the floor
 
 
+def _log_mel_numpy(y, n_mels):
+    """Independent numpy statement of src/audio.rs:147-237 (rfft instead of the direct DFT, f64 throughout): reflect
+    padding of 200, periodic Hann window, |X|^2, Slaney-style filterbank with area normalisation, log10 floor 1e-10,
+    max - 8 clamp, (x + 4) / 4; frames past the audio at the floor."""
+    sr, n_fft, hop, n_frames = 16000, 400, 160, 3000
+    x = np.zeros(30 * sr, np.float64)
+    n = min(len(y), 30 * sr)
+    x[:n] = y[:n]
+    xp = np.pad(x, (n_fft // 2, n_fft // 2), mode="reflect")
+    win = 0.5 - 0.5 * np.cos(2 * np.pi * np.arange(n_fft) / n_fft)
+    live = min((n + n_fft // 2 + hop - 1) // hop, n_frames)
+    frames = np.stack([xp[t * hop:t * hop + n_fft] * win for t in range(live)])
+    power = np.abs(np.fft.rfft(frames, axis=1)) ** 2
+    logstep = 27.0 / np.log(6.4)
+
+    def hz_to_mel(f):
+        return 15.0 + np.log(f / 1000.0) * logstep if f >= 1000.0 else 3.0 * f / 200.0
+
+    def mel_to_hz(mm):
+        return 1000.0 * np.exp((mm - 15.0) / logstep) if mm >= 15.0 else 200.0 * mm / 3.0
+
+    fft_f = np.arange(n_fft // 2 + 1) * (sr / 2.0) / (n_fft // 2)
+    m0, m1 = hz_to_mel(0.0), hz_to_mel(8000.0)
+    ff = np.array([mel_to_hz(m0 + (m1 - m0) * i / (n_mels + 1)) for i in range(n_mels + 2)])
+    fb = np.zeros((n_mels, n_fft // 2 + 1))
+    for i in range(n_mels):
+        down = (fft_f - ff[i]) / (ff[i + 1] - ff[i])
+        up = (ff[i + 2] - fft_f) / (ff[i + 2] - ff[i + 1])
+        fb[i] = np.maximum(np.minimum(down, up), 0.0) * 2.0 / (ff[i + 2] - ff[i])
+    out = np.full((n_mels, n_frames), -10.0)
+    out[:, :live] = np.log10(np.maximum(fb @ power.T, 1e-10))
+    return (np.maximum(out, out.max() - 8.0) + 4.0) / 4.0
+
+
+@pytest.mark.parametrize("seed,n", [(5, 480000), (6, 123457), (7, 3000)])
+def test_log_mel_matches_an_independent_numpy_statement(seed, n):
+    y = m.synth_clip(seed, n)
+    mel, frames = m.log_mel(y, 128)
+    want = _log_mel_numpy(y, 128)
+    assert frames == min((n + 159) // 160, 3000)
+    # f32 power and filterbank sums against f64 throughout: well inside the fp16 step the encoder reads them with
+    assert np.abs(mel - want).max() < 1e-4
+
+
 def test_synth_clip_is_seeded():
     a, b, c = m.synth_clip(3, 16000), m.synth_clip(3, 16000), m.synth_clip(4, 16000)
     assert np.array_equal(a, b) and not np.array_equal(a, c) and np.abs(a).max() <= 1.0
