@@ -24,7 +24,7 @@ namespace mmz {
 
 constexpr int XCH = 64;                       // reference chunk (kernels/whisper.cu:360)
 constexpr int XNCH = (TENC + XCH - 1) / XCH;  // 24 chunks
-constexpr int XCPC = 3;                       // reference chunks per CTA (1: 66 us, 2: 51.1 us, 3: 50.6 us per layer)
+constexpr int XCPC = 3;                       // reference chunks per CTA (1: 66, 2: 51.1, 3: 49.3, 4: 51.0 us per layer)
 constexpr int XCL = XNCH / XCPC;              // CTAs per (sequence, head)
 constexpr int XPER = XCPC * XCH;              // positions per CTA
 static_assert(XNCH % XCPC == 0 && XCPC <= 4, "whole chunks per CTA, one warp per chunk for the statistics");
