@@ -277,8 +277,10 @@ __global__ void __launch_bounds__(128, 8) cross_pv_kernel(const h16* __restrict_
                                                   // the group partials
     __shared__ float p[XPER];
     __shared__ float2 gs[XNCH];
+    __shared__ float2 gms;  // the global (max, sum)
     __shared__ uint64_t bar[XCPC];
     static_assert(XCPC * 16 * HD * 4 <= XPER * HD * 2, "the group partials fit in the V slice");
+    static_assert(XNCH <= 32, "one lane per chunk");
     __shared__ int abort;
     griddep_launch_dependents();  // the combine kernel may be scheduled as soon as every CTA here is resident
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
@@ -301,14 +303,20 @@ __global__ void __launch_bounds__(128, 8) cross_pv_kernel(const h16* __restrict_
     if (t < XNCH) gs[t] = __ldcg(&xs.stat[(long)bh * XNCH + t]);
     for (int jj = t; jj < n; jj += 128) p[jj] = __ldcg(&xs.S[(long)bh * TENC + j0 + jj]);
     __syncthreads();
-    // the global max and sum over the 24 chunks in order (kernels/whisper.cu:414-417)
-    float m = -INFINITY;
-    for (int c = 0; c < XNCH; c++) m = fmaxf(m, gs[c].x);
-    float sum = 0.f;
-    for (int c = 0; c < XNCH; c++) {
-        float2 g2 = gs[c];
-        sum += g2.y * expf(g2.x - m);
+    // the global max and sum over the 24 chunks in order (kernels/whisper.cu:414-417), formed once by warp 0: lane c
+    // takes chunk c's exponential, and the sum runs through the chunks in order as fused multiply-adds
+    if (t < 32) {
+        const float2 g2 = t < XNCH ? gs[t] : make_float2(-INFINITY, 0.f);
+        float mx = g2.x;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
+        const float e = t < XNCH ? expf(g2.x - mx) : 0.f;
+        float sm = 0.f;
+        for (int c = 0; c < XNCH; c++)
+            sm = __fmaf_rn(__shfl_sync(0xffffffff, g2.y, c), __shfl_sync(0xffffffff, e, c), sm);
+        if (t == 0) gms = make_float2(mx, sm);
     }
+    __syncthreads();
+    const float m = gms.x, sum = gms.y;
     const int slot = aslot[layer * nh + hh];
     h16* arow = slot >= 0 ? align + (((long)b * maxT + ctr[0]) * na + slot) * TENC + j0 : nullptr;
     for (int jj = t; jj < n; jj += 128) {
