@@ -358,6 +358,11 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         return;
     }
     ws_ = alloc(WS_BYTES);
+    if (cudaMallocHost(&done_host_, (size_t)bmax_ * 4) != cudaSuccess ||
+        cudaEventCreateWithFlags(&poll_ev_, cudaEventDisableTiming) != cudaSuccess) {
+        err_ = "pinned poll buffer / event setup failed";
+        return;
+    }
     if (k_->native() && cublasLtCreate(&lt_) != CUBLAS_STATUS_SUCCESS) {
         err_ = "cuBLASLt setup failed";
         return;
@@ -460,6 +465,8 @@ Engine::~Engine() {
     for (void* p : allocs_) cudaFree(p);
     if (blas_) cublasDestroy(blas_);
     if (lt_) cublasLtDestroy(lt_);
+    if (poll_ev_) cudaEventDestroy(poll_ev_);
+    if (done_host_) cudaFreeHost(done_host_);
     if (st_) cudaStreamDestroy(st_);
 }
 
@@ -774,18 +781,26 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
     for (int s = 0; s < n; s++) std::memcpy(&prompts[(size_t)s * np], prompt, np * 4);
     CK(reset(prompts.data(), n, np));
     if (graph && (graph_b_ != n || graph_np_ != np || !graph_)) CK(capture(n, np));
+    // src/transcribe.rs:123-142 polls `done` every 8 steps. Here the poll reads the copy recorded 8 steps earlier, which
+    // has landed while those steps were queued behind it, so the stream never drains for a poll; a batch whose
+    // sequences have all finished may then run up to 8 more steps, which write only end-of-text tokens after the first
+    // one and change no output.
     int steps = 0;
-    std::vector<int> dn(n);
+    bool polled = false;
     while (steps < max_steps) {
         if (graph) CK(replay());
         else CK(step(n, np));
         steps++;
         if (steps % 8 == 0 && steps >= np) {
-            CUDA_CK(cudaMemcpyAsync(dn.data(), done_, (size_t)n * 4, cudaMemcpyDeviceToHost, st_));
-            CUDA_CK(cudaStreamSynchronize(st_));
-            bool all = true;
-            for (int v : dn) all = all && v != 0;
-            if (all) break;
+            if (polled) {
+                CUDA_CK(cudaEventSynchronize(poll_ev_));
+                bool all = true;
+                for (int s = 0; s < n; s++) all = all && done_host_[s] != 0;
+                if (all) break;
+            }
+            CUDA_CK(cudaMemcpyAsync(done_host_, done_, (size_t)n * 4, cudaMemcpyDeviceToHost, st_));
+            CUDA_CK(cudaEventRecord(poll_ev_, st_));
+            polled = true;
         }
     }
     CUDA_CK(cudaStreamSynchronize(st_));

@@ -141,6 +141,8 @@ class Engine {
     int* rc_ = nullptr;      // native image: token rows and frame columns per clip for the cost kernel
     float* tms_ = nullptr;   // native image: the token start times [bmax][max_t] from the GPU DTW
     size_t d2h_bytes_ = 0;   // bytes the last transcribe copied device -> host
+    int* done_host_ = nullptr;       // pinned copy of done for the decoding loop's poll
+    cudaEvent_t poll_ev_ = nullptr;  // recorded after that copy
     int *tok_, *done_, *ctr_, *aslot_;
     unsigned char *sup_;
     float* mel32_;
