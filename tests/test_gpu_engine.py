@@ -160,3 +160,22 @@ def test_transcribe_graph_matches_eager(cuda):
     assert np.array_equal(g["tokens"], x["tokens"]) and np.array_equal(g["times"], x["times"])
     assert (g["lens"] == len(cfg.prompt) + 24).all()
     e.close()
+
+
+def test_transcribe_stops_once_every_sequence_has_finished(cuda):
+    """With every token but end-of-text suppressed, each sequence finishes at its first generated token: the decoding
+    loop stops at a poll (the steps it may run past that change nothing), graph and eager agree, and every length is
+    the prompt plus one."""
+    import mimizuku_b200 as m
+    cfg = m.TINY
+    b = 3
+    mel, frames = _clips(b, cfg.n_mels, seed=4)
+    sup = [t for t in range(cfg.vocab) if t != cfg.eos]
+    e = m.Engine(cfg, bmax=b, eg=2, seed=6, suppress=sup)
+    g = e.transcribe(mel, frames, max_new=200, graph=True)
+    x = e.transcribe(mel, frames, max_new=200, graph=False)
+    np_ = len(cfg.prompt)
+    assert (g["lens"] == np_ + 1).all() and (x["lens"] == np_ + 1).all()
+    assert (g["tokens"][:, np_] == cfg.eos).all()
+    assert np.array_equal(g["tokens"], x["tokens"]) and np.array_equal(g["times"], x["times"])
+    e.close()
