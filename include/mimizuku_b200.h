@@ -180,6 +180,13 @@ void mmz_engine_destroy(mmz_engine* e);
 int mmz_engine_transcribe(mmz_engine* e, const float* mel, const int* frames, int n, const int* prompt, int np,
                           int max_steps, int use_graph, int threads, int* tokens, int* lens, float* times,
                           double* stage_s);
+/* The whole of src/transcribe.rs:25-167 from host audio: ys[s] holds ns[s] samples at 16 kHz (the first 30 s are
+ * used); the log-mel features are computed on the GPU (mmz_log_mel_gpu) group by group and fed to the encoder, then as
+ * mmz_engine_transcribe. frames [n] receives each clip's 10 ms frames that hold audio (as mmz_log_mel_batch returns
+ * them); stage_s[0] covers the features and the encoder. Native kernel image only. */
+int mmz_engine_transcribe_audio(mmz_engine* e, const float* const* ys, const long* ns, int n, const int* prompt, int np,
+                                int max_steps, int use_graph, int threads, int* tokens, int* lens, float* times,
+                                int* frames, double* stage_s);
 /* Engine::encode (src/model.rs:545-625) for gn <= eg clips of fp16 log-mel already on the device. */
 int mmz_engine_encode(mmz_engine* e, const void* mel16, int gn, int slot0);
 /* Engine::reset (src/model.rs:628-637): prompts [b][np]. */

@@ -76,6 +76,8 @@ SIGNATURES = {
                                _ULL]),
     "mmz_engine_destroy": (None, [_P]),
     "mmz_engine_transcribe": (_I, [_P, _FP, _IP, _I, _IP, _I, _I, _I, _I, _IP, _IP, _FP, _DP]),
+    "mmz_engine_transcribe_audio": (_I, [_P, ctypes.POINTER(_FP), ctypes.POINTER(_L), _I, _IP, _I, _I, _I, _I, _IP,
+                                         _IP, _FP, _IP, _DP]),
     "mmz_engine_encode": (_I, [_P, _P, _I, _I]),
     "mmz_engine_reset": (_I, [_P, _IP, _I, _I]),
     "mmz_engine_step": (_I, [_P, _I, _I]),

@@ -195,6 +195,15 @@ int mmz_engine_transcribe(mmz_engine* e, const float* mel, const int* frames, in
     return e->e->transcribe(mel, frames, n, prompt, np, max_steps, use_graph != 0, threads, tokens, lens, times, stage_s);
 }
 
+int mmz_engine_transcribe_audio(mmz_engine* e, const float* const* ys, const long* ns, int n, const int* prompt, int np,
+                                int max_steps, int use_graph, int threads, int* tokens, int* lens, float* times,
+                                int* frames, double* stage_s) {
+    if (!e) return fail("null engine");
+    if (!ys || !ns || !frames) return fail("transcribe_audio: null clip, length or frames array");
+    return e->e->transcribe_audio(ys, ns, n, prompt, np, max_steps, use_graph != 0, threads, tokens, lens, times,
+                                  frames, stage_s);
+}
+
 int mmz_engine_encode(mmz_engine* e, const void* mel16, int gn, int slot0) {
     return e ? e->e->encode_dev(mel16, gn, slot0) : fail("null engine");
 }

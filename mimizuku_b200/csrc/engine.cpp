@@ -762,13 +762,10 @@ int Engine::replay() {
 // transcribe.rs:104-167
 int Engine::transcribe(const float* mel, const int* frames, int n, const int* prompt, int np, int max_steps,
                        bool graph, int threads, int* tokens, int* lens, float* times, double* stage_s) {
-    using clk = std::chrono::steady_clock;
-    const int mt = dm_.max_t, nm = dm_.n_mels, na = (int)gc_.align_heads.size();
     if (n < 1 || n > bmax_) return fail("transcribe: 1..bmax clips per call");
-    if (max_steps < 1 || max_steps > mt - 1) max_steps = mt - 1;
-    auto t0 = clk::now();
+    const auto t0 = std::chrono::steady_clock::now();
     // fp32 log-mel to the device, rounded to fp16 there (the reference rounds on the host with f2h, model.rs:549)
-    const size_t per = (size_t)nm * NFRAMES;
+    const size_t per = (size_t)dm_.n_mels * NFRAMES;
     for (int g0 = 0; g0 < n; g0 += eg_) {
         const int gn = std::min(eg_, n - g0);
         CUDA_CK(cudaMemcpyAsync(mel32_, mel + per * g0, per * gn * 4, cudaMemcpyHostToDevice, st_));
@@ -776,6 +773,51 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
         CK(encode_dev(mel_, gn, g0));
     }
     CUDA_CK(cudaStreamSynchronize(st_));
+    return decode_and_times(frames, n, prompt, np, max_steps, graph, threads, tokens, lens, times, stage_s, t0);
+}
+
+// The same pipeline from host audio: each group's samples to the device, log-mel there (logmel.cu: the host
+// restatement's power spectra, log10 rounded once), then as above. frames [n] receives the 10 ms frames that hold audio.
+int Engine::transcribe_audio(const float* const* ys, const long* ns, int n, const int* prompt, int np, int max_steps,
+                             bool graph, int threads, int* tokens, int* lens, float* times, int* frames,
+                             double* stage_s) {
+    if (n < 1 || n > bmax_) return fail("transcribe_audio: 1..bmax clips per call");
+    if (!k_->native()) return fail("transcribe_audio: needs the native kernel image (log-mel on the GPU)");
+    const auto t0 = std::chrono::steady_clock::now();
+    if (!audio_) {  // first call: device staging for one encoder group
+        audio_ = (float*)alloc((size_t)eg_ * N_SAMPLES * 4);
+        alens_ = (int*)alloc((size_t)eg_ * 4);
+        lmw_bytes_ = log_mel_work_bytes(eg_);
+        lmw_ = alloc(lmw_bytes_);
+        if (!audio_ || !alens_ || !lmw_) return fail("transcribe_audio: device memory allocation failed");
+    }
+    std::vector<int> lens32(eg_);
+    for (int g0 = 0; g0 < n; g0 += eg_) {
+        const int gn = std::min(eg_, n - g0);
+        for (int c = 0; c < gn; c++) {
+            const long len = std::max(0L, std::min(ns[g0 + c], N_SAMPLES));
+            lens32[c] = (int)len;
+            if (len > 0)
+                CUDA_CK(cudaMemcpyAsync(audio_ + (size_t)c * N_SAMPLES, ys[g0 + c], (size_t)len * 4,
+                                        cudaMemcpyHostToDevice, st_));
+        }
+        CUDA_CK(cudaMemcpyAsync(alens_, lens32.data(), (size_t)gn * 4, cudaMemcpyHostToDevice, st_));
+        CK(launch_log_mel(audio_, alens_, gn, dm_.n_mels, mel32_, lmw_, lmw_bytes_, st_));
+        CK(launch_f32_to_f16(mel32_, mel_, (long)((size_t)dm_.n_mels * NFRAMES * gn), st_));
+        CK(encode_dev(mel_, gn, g0));
+        CUDA_CK(cudaStreamSynchronize(st_));  // lens32 and the staging buffers are reused by the next group
+    }
+    for (int s = 0; s < n; s++) frames[s] = (int)std::min((std::max(0L, std::min(ns[s], N_SAMPLES)) + HOP - 1) / HOP,
+                                                          (long)NFRAMES);
+    return decode_and_times(frames, n, prompt, np, max_steps, graph, threads, tokens, lens, times, stage_s, t0);
+}
+
+int Engine::decode_and_times(const int* frames, int n, const int* prompt, int np, int max_steps, bool graph,
+                             int threads, int* tokens, int* lens, float* times, double* stage_s,
+                             std::chrono::steady_clock::time_point t0) {
+    using clk = std::chrono::steady_clock;
+    const int mt = dm_.max_t, na = (int)gc_.align_heads.size();
+    if (max_steps < 1 || max_steps > mt - 1) max_steps = mt - 1;
     auto t1 = clk::now();
     std::vector<int> prompts((size_t)n * np);
     for (int s = 0; s < n; s++) std::memcpy(&prompts[(size_t)s * np], prompt, np * 4);

@@ -13,6 +13,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <memory>
 #include <string>
 #include <utility>
@@ -64,6 +65,10 @@ class Engine {
     // stage_s = {encode, decode, timestamps} seconds
     int transcribe(const float* mel, const int* frames, int n, const int* prompt, int np, int max_steps, bool graph,
                    int threads, int* tokens, int* lens, float* times, double* stage_s);
+    // the same from host audio (ys[s]: ns[s] samples at 16 kHz, the first 30 s are used): log-mel on the GPU (native
+    // image only); frames [n] receives each clip's 10 ms frames that hold audio; stage_s[0] includes the features
+    int transcribe_audio(const float* const* ys, const long* ns, int n, const int* prompt, int np, int max_steps,
+                         bool graph, int threads, int* tokens, int* lens, float* times, int* frames, double* stage_s);
 
     void* buffer(const std::string& name) const;
     cudaStream_t stream() const { return st_; }
@@ -90,6 +95,9 @@ class Engine {
     int matmul(bool ta, bool tb, int m, int n, int k, float alpha, const void* a, int lda, long long sa, const void* b,
                int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch);
     void* alloc(size_t bytes);
+    int decode_and_times(const int* frames, int n, const int* prompt, int np, int max_steps, bool graph, int threads,
+                         int* tokens, int* lens, float* times, double* stage_s,
+                         std::chrono::steady_clock::time_point t0);
     void* dec_out(int layer, int which) const;
     int init_weights(unsigned long long seed);
 
@@ -142,6 +150,10 @@ class Engine {
     float* tms_ = nullptr;   // native image: the token start times [bmax][max_t] from the GPU DTW
     size_t d2h_bytes_ = 0;   // bytes the last transcribe copied device -> host
     int* done_host_ = nullptr;       // pinned copy of done for the decoding loop's poll
+    float* audio_ = nullptr;         // transcribe_audio: one encoder group's samples [eg][480000]
+    int* alens_ = nullptr;           // and their lengths
+    void* lmw_ = nullptr;            // log-mel work space
+    size_t lmw_bytes_ = 0;
     cudaEvent_t poll_ev_ = nullptr;  // recorded after that copy
     int *tok_, *done_, *ctr_, *aslot_;
     unsigned char *sup_;

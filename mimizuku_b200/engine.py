@@ -103,6 +103,29 @@ class Engine:
                                          times.ctypes.data_as(_FP), stage.ctypes.data_as(_DP)), "transcribe")
         return {"tokens": tokens, "lens": lens, "times": times, "stage_s": stage}
 
+    def transcribe_audio(self, clips, prompt=None, max_new=None, graph=True, threads=0):
+        """src/transcribe.rs:25-167 from host audio: clips is a list of float32 sample arrays at 16 kHz (n <= bmax);
+        the log-mel features are computed on the GPU. Returns transcribe's dict plus frames [n]."""
+        clips = [np.ascontiguousarray(c, dtype=np.float32) for c in clips]
+        n = len(clips)
+        prompt = np.asarray(prompt if prompt is not None else self.cfg.prompt, dtype=np.int32)
+        np_ = len(prompt)
+        mt = self.cfg.max_t
+        max_steps = 0 if max_new is None else min(mt - 1, np_ - 1 + max_new)
+        ptrs = (_FP * n)(*[c.ctypes.data_as(_FP) for c in clips])
+        lens_in = (ctypes.c_long * n)(*[len(c) for c in clips])
+        tokens = np.zeros((n, mt), np.int32)
+        lens = np.zeros(n, np.int32)
+        times = np.zeros((n, mt), np.float32)
+        frames = np.zeros(n, np.int32)
+        stage = np.zeros(3, np.float64)
+        _check(lib.mmz_engine_transcribe_audio(self._h, ptrs, lens_in, n, prompt.ctypes.data_as(_IP), np_, max_steps,
+                                               int(graph), threads, tokens.ctypes.data_as(_IP),
+                                               lens.ctypes.data_as(_IP), times.ctypes.data_as(_FP),
+                                               frames.ctypes.data_as(_IP), stage.ctypes.data_as(_DP)),
+               "transcribe_audio")
+        return {"tokens": tokens, "lens": lens, "times": times, "frames": frames, "stage_s": stage}
+
     def encode(self, mel16, gn, slot0=0):
         """Engine::encode (src/model.rs:545-625) of gn clips of fp16 log-mel at device address mel16."""
         _check(lib.mmz_engine_encode(self._h, mel16 if isinstance(mel16, int) else mel16.data_ptr(), gn, slot0),

@@ -179,3 +179,27 @@ def test_transcribe_stops_once_every_sequence_has_finished(cuda):
     assert (g["tokens"][:, np_] == cfg.eos).all()
     assert np.array_equal(g["tokens"], x["tokens"]) and np.array_equal(g["times"], x["times"])
     e.close()
+
+
+def test_transcribe_from_audio_is_transcribe_of_the_gpu_features(cuda):
+    """mmz_engine_transcribe_audio (features on the GPU, group by group) gives exactly what mmz_engine_transcribe gives
+    for the features of mmz_log_mel_gpu, with the host's frame counts."""
+    import mimizuku_b200 as m
+    torch = cuda
+    cfg = m.TINY
+    b = 3
+    ys = [m.synth_clip(20 + i, 16000 * (5 + 9 * i)) for i in range(b)]
+    e = m.Engine(cfg, bmax=b, eg=2, seed=8, suppress=[cfg.eos])
+    r = e.transcribe_audio(ys, max_new=16)
+    audio = np.zeros((b, 480000), np.float32)
+    for i, y in enumerate(ys):
+        audio[i, :len(y)] = y
+    mel = torch.empty((b, cfg.n_mels, 3000), dtype=torch.float32, device="cuda")
+    m.log_mel_gpu(torch.from_numpy(audio).cuda(), torch.tensor([len(y) for y in ys], dtype=torch.int32,
+                                                               device="cuda"), cfg.n_mels, mel)
+    _, frames = m.log_mel_batch(ys, cfg.n_mels)
+    assert np.array_equal(r["frames"], frames)
+    x = e.transcribe(mel.cpu().numpy(), frames, max_new=16)
+    for k in ("tokens", "lens", "times"):
+        assert np.array_equal(r[k], x[k]), k
+    e.close()
