@@ -9,11 +9,12 @@
 //   warp 1      MMA issuer (one thread): S = Q K^T (M128 N128 K64) into TMEM, then O += P V (M128 N64 K128) with P
 //               read from TMEM and V as an MN-major shared-memory operand; completion is signalled with
 //               tcgen05.commit
-//   warps 2-9   softmax: query row i of the tile (TMEM lane i) is shared by two threads, one per half of the 128
-//               keys of a tile (warps 2-5: keys 0-63, warps 6-9: keys 64-127). Each loads its 64 scores from TMEM
-//               into registers (which frees S for the next QK product at once), exchanges its row maximum with its
-//               partner through shared memory, keeps its share of the row sum, writes its 64 probabilities (fp16)
-//               into TMEM for the P.V product and rescales its 32 columns of the O row when the maximum moves
+//   warps 2-9   softmax: a warp owns 16 query rows (TMEM lanes) and loads their scores with the 16x256b shape, so
+//               thread t holds rows t / 4 and t / 4 + 8 of them, two keys of every 8-key block: the 4 threads of a
+//               row are lanes of one warp and agree on its maximum through two shuffles. Each loads its 64 scores
+//               from TMEM into registers (which frees S for the next QK product at once), keeps its share of the
+//               two row sums, writes its 32 packed probabilities (fp16) into TMEM with the matching 16x128b shape
+//               for the P.V product and rescales its columns of the two O rows when a maximum moves
 // TMEM holds S (columns 0-127), O (128-191) and P (192-255): 256 columns, so two CTAs share an SM and the softmax
 // warps of one overlap the MMAs and copies of the other (16 softmax warps per SM).
 //
@@ -51,10 +52,8 @@ struct Smem {
     uint8_t q[TILE];
     uint8_t k[KST][TILE];
     uint8_t v[VST][TILE];
-    float xmax[2][2][BM];                    // [tile parity][key half][row]: the partners' row maxima, then sums
     uint64_t bar_q, bar_kf[KST], bar_ke[KST], bar_vf[VST], bar_ve[VST];
     uint64_t bar_sf, bar_sfree, bar_pf, bar_od, bar_fin;
-    uint64_t bar_x[4];                       // per lane quarter: the two threads of a row have exchanged a value
     uint32_t tmem;
     int abort;
 };
@@ -98,7 +97,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         mbar_init(&s.bar_pf, 8);
         mbar_init(&s.bar_od, 1);
         mbar_init(&s.bar_fin, 1);
-        for (int i = 0; i < 4; i++) mbar_init(&s.bar_x[i], 2);  // the two warps of a lane quarter
         fence_mbar_init();
     }
     if (warp == 0) {
@@ -187,91 +185,101 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             umma_commit(&s.bar_fin);  // completes once every MMA issued above has finished
         }
     } else {
-        // ---------------------------------------------------------------- softmax (warps 2..9, two threads per row)
+        // ---------------------------------------------------------------- softmax (warps 2..9)
+        // A warp owns 16 query rows (TMEM lanes) of its lane quarter and reads them with the 16x256b shape: thread t
+        // holds rows t / 4 and t / 4 + 8 of those 16, two columns of every 8-column block, so the 4 threads sharing a
+        // row are lanes of one warp and meet through shuffles.
         const int quarter = warp & 3;        // a warp may only touch TMEM lanes 32 * (warp % 4) .. + 31
-        const int hf = (warp - 2) >> 2;      // key half of the tile
-        const int row = quarter * 32 + lane;
-        const uint32_t loff = (uint32_t)(quarter * 32) << 16;
-        const uint32_t tSh = tS + loff + hf * 64, tPh = tP + loff + hf * 32, tOh = tO + loff + hf * 32;
+        const int sub16 = (warp - 2) >> 2;   // which 16 lanes of the quarter
+        const int q4 = lane & 3, rl = lane >> 2;
+        const int row0 = quarter * 32 + sub16 * 16 + rl;  // and row0 + 8
+        const uint32_t tl = tbase + ((uint32_t)(quarter * 32 + sub16 * 16) << 16);
         const float sl2 = 0.125f * 1.4426950408889634f;  // 0.125 * log2(e)
         const float2 sl2_2 = make_float2(sl2, sl2);
-        float m = -INFINITY, l = 0.f;
+        float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
         bool ok = true;
         for (int j = 0; j < NKT; j++) {
-            const bool last = j == NKT - 1 && hf == 1;  // keys 92.. of the last tile are past 1500
             ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_sf, j & 1, abort, limit_ns, status, K_ENC, 30));
             if (!ok) break;
             tc_fence_after();
-            uint32_t raw[64];
-            tmem_ld64(tSh, raw);
+            uint32_t raw[64];  // block b: [4b, 4b + 1] row0, [4b + 2, 4b + 3] row0 + 8, keys 8b + 2 q4 + {0, 1}
+            tmem_ld_16x256b_x16(tl + (tS - tbase), raw);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s.bar_sfree);  // the warp's scores are in registers: the next QK may start
             float* sv = reinterpret_cast<float*>(raw);
-            if (last) {
+            if (j == NKT - 1) {  // keys past 1500 (zero-filled K rows)
 #pragma unroll
-                for (int c = LAST_VALID - 64; c < 64; c++) sv[c] = -INFINITY;
-            }
-            // the maximum of this thread's 64 scores, four chains
-            float a0 = fmaxf(sv[0], sv[1]), a1 = fmaxf(sv[2], sv[3]), a2 = fmaxf(sv[4], sv[5]), a3 = fmaxf(sv[6], sv[7]);
+                for (int b = 0; b < 16; b++)
 #pragma unroll
-            for (int c = 8; c < 64; c += 8) {
-                a0 = fmax3(a0, sv[c], sv[c + 1]);
-                a1 = fmax3(a1, sv[c + 2], sv[c + 3]);
-                a2 = fmax3(a2, sv[c + 4], sv[c + 5]);
-                a3 = fmax3(a3, sv[c + 6], sv[c + 7]);
+                    for (int e = 0; e < 2; e++)
+                        if (8 * b + 2 * q4 + e >= LAST_VALID) sv[4 * b + e] = sv[4 * b + 2 + e] = -INFINITY;
             }
-            float tmax = fmaxf(fmaxf(a0, a1), fmaxf(a2, a3));
-            // exchange with the partner thread of this row (the other key half)
-            s.xmax[j & 1][hf][row] = tmax;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.bar_x[quarter]);
-            ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_x[quarter], j & 1, abort, limit_ns, status, K_ENC, 33));
-            if (!ok) break;
-            tmax = fmaxf(tmax, s.xmax[j & 1][hf ^ 1][row]) * sl2;
+            // the row maxima: this thread's 32 scores of each row, then the row's 4 threads
+            float mx[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float a0 = fmaxf(sv[2 * h], sv[2 * h + 1]), a1 = fmaxf(sv[4 + 2 * h], sv[5 + 2 * h]);
+#pragma unroll
+                for (int b = 2; b < 16; b += 2) {
+                    a0 = fmax3(a0, sv[4 * b + 2 * h], sv[4 * b + 2 * h + 1]);
+                    a1 = fmax3(a1, sv[4 * b + 4 + 2 * h], sv[4 * b + 5 + 2 * h]);
+                }
+                mx[h] = fmaxf(a0, a1);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
+                mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2)) * sl2;
+            }
             // the running maximum only moves when the tile's exceeds it by more than 8 (log2 units): the
             // probabilities then stay below 2^8 (exact in fp16), and the O row is rescaled far less often
-            const float mn = tmax > m + 8.f ? tmax : m;
-            const float corr = mn == m ? 1.f : ex2_approx(m - mn);
-            m = mn;
-            const float2 nmn2 = make_float2(-mn, -mn);
-            float2 rs2 = make_float2(0.f, 0.f), rs2b = make_float2(0.f, 0.f);
-            // exponentials (a quarter of the pairs on the FMA pipe), P into TMEM in two halves
+            float corr[2];
+            float2 nmn2[2];
 #pragma unroll
-            for (int h2 = 0; h2 < 2; h2++) {
-                uint32_t pk[16];
+            for (int h = 0; h < 2; h++) {
+                const float mn = mx[h] > m[h] + 8.f ? mx[h] : m[h];
+                corr[h] = mn == m[h] ? 1.f : ex2_approx(m[h] - mn);
+                m[h] = mn;
+                nmn2[h] = make_float2(-mn, -mn);
+            }
+            // exponentials (a quarter of the blocks on the FMA pipe), packed P in the 16x128b mapping: register 2b
+            // row0, 2b + 1 row0 + 8, column 4b + q4 = keys 8b + 2 q4, 8b + 2 q4 + 1
+            float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            uint32_t pk[32];
 #pragma unroll
-                for (int c = 0; c < 16; c++) {
-                    const int cc = h2 * 16 + c;
-                    const float2 x = ffma2(make_float2(sv[2 * cc], sv[2 * cc + 1]), sl2_2, nmn2);
+            for (int b = 0; b < 16; b++)
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const float2 x = ffma2(make_float2(sv[4 * b + 2 * h], sv[4 * b + 2 * h + 1]), sl2_2, nmn2[h]);
                     float2 e;
-                    if ((POLY_PAIRS >> c) & 1) {
+                    if ((b & 3) == 3) {
                         e = exp2_poly2(x);
                     } else {
                         e.x = ex2_approx(x.x);
                         e.y = ex2_approx(x.y);
                     }
-                    if (c & 1) rs2b = fadd2(rs2b, e);
-                    else rs2 = fadd2(rs2, e);
-                    pk[c] = pack_h2(e.x, e.y);
+                    rs[h] = fadd2(rs[h], e);
+                    pk[2 * b + h] = pack_h2(e.x, e.y);
                 }
-                if (h2 == 0 && j > 0) {
-                    // P.V of the previous tile must be complete: it reads the P columns and accumulates into O
-                    ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_od, (j - 1) & 1, abort, limit_ns, status, K_ENC, 31));
-                    if (!ok) break;
-                    tc_fence_after();
-                }
-                tmem_st16(tPh + h2 * 16, pk);
-            }
-            if (!ok) break;
-            l = l * corr + ((rs2.x + rs2.y) + (rs2b.x + rs2b.y));
-            // the running max moved: rescale this thread's 32 columns of the O row before the next P.V
-            if (j > 0 && __any_sync(0xffffffff, corr != 1.f)) {
-                uint32_t r[32];
-                tmem_ld32(tOh, r);
 #pragma unroll
-                for (int i = 0; i < 32; i++) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-                tmem_st32(tOh, r);
+            for (int h = 0; h < 2; h++) l[h] = l[h] * corr[h] + (rs[h].x + rs[h].y);
+            if (j > 0) {
+                // P.V of the previous tile must be complete: it reads the P columns and accumulates into O
+                ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_od, (j - 1) & 1, abort, limit_ns, status, K_ENC, 31));
+                if (!ok) break;
+                tc_fence_after();
+            }
+            tmem_st_16x128b_x16(tl + (tP - tbase), pk);
+            // the running max moved: rescale the two O rows before the next P.V
+            if (j > 0 && __any_sync(0xffffffff, corr[0] != 1.f || corr[1] != 1.f)) {
+                uint32_t r[32];
+                tmem_ld_16x256b_x8(tl + (tO - tbase), r);
+#pragma unroll
+                for (int b = 0; b < 8; b++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) r[4 * b + e] = __float_as_uint(__uint_as_float(r[4 * b + e]) * corr[e >> 1]);
+                tmem_st_16x256b_x8(tl + (tO - tbase), r);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -280,25 +288,26 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         }
         if (ok) ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_od, (NKT - 1) & 1, abort, limit_ns, status, K_ENC, 32));
         if (ok) {
-            // the row sum is the two halves' shares
-            s.xmax[NKT & 1][hf][row] = l;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s.bar_x[quarter]);
-            ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_x[quarter], NKT & 1, abort, limit_ns, status, K_ENC, 34));
-        }
-        if (ok) {
-            const float lt = l + s.xmax[NKT & 1][hf ^ 1][row];
+            // the row sums are the row's 4 threads' shares
+            float lt[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                lt[h] = l[h] + __shfl_xor_sync(0xffffffff, l[h], 1);
+                lt[h] += __shfl_xor_sync(0xffffffff, lt[h], 2);
+            }
             tc_fence_after();
-            const int qrow = qt * BM + row;
             uint32_t r[32];
-            tmem_ld32(tOh, r);
-            uint32_t o[16];
+            tmem_ld_16x256b_x8(tl + (tO - tbase), r);
 #pragma unroll
-            for (int i = 0; i < 16; i++) o[i] = pack_h2(__uint_as_float(r[2 * i]) / lt, __uint_as_float(r[2 * i + 1]) / lt);
-            if (qrow < TENC) {
-                uint4* dst = reinterpret_cast<uint4*>(out + ((long)g * TENC + qrow) * d + hh * HD + hf * 32);
+            for (int h = 0; h < 2; h++) {
+                const int qrow = qt * BM + row0 + 8 * h;
+                if (qrow < TENC) {
+                    uint32_t* dst = reinterpret_cast<uint32_t*>(out + ((long)g * TENC + qrow) * d + hh * HD + 2 * q4);
 #pragma unroll
-                for (int i = 0; i < 4; i++) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    for (int b = 0; b < 8; b++)
+                        dst[4 * b] = pack_h2(__uint_as_float(r[4 * b + 2 * h]) / lt[h],
+                                             __uint_as_float(r[4 * b + 2 * h + 1]) / lt[h]);
+                }
             }
         }
     }
