@@ -244,33 +244,39 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                 nmn2[h] = make_float2(-mn, -mn);
             }
             // exponentials (a quarter of the blocks on the FMA pipe), packed P in the 16x128b mapping: register 2b
-            // row0, 2b + 1 row0 + 8, column 4b + q4 = keys 8b + 2 q4, 8b + 2 q4 + 1
+            // row0, 2b + 1 row0 + 8, column 4b + q4 = keys 8b + 2 q4, 8b + 2 q4 + 1; stored in two halves
             float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-            uint32_t pk[32];
 #pragma unroll
-            for (int b = 0; b < 16; b++)
+            for (int hb = 0; hb < 2; hb++) {
+                uint32_t pk[16];
 #pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const float2 x = ffma2(make_float2(sv[4 * b + 2 * h], sv[4 * b + 2 * h + 1]), sl2_2, nmn2[h]);
-                    float2 e;
-                    if ((b & 3) == 3) {
-                        e = exp2_poly2(x);
-                    } else {
-                        e.x = ex2_approx(x.x);
-                        e.y = ex2_approx(x.y);
+                for (int bb = 0; bb < 8; bb++)
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int b = hb * 8 + bb;
+                        const float2 x = ffma2(make_float2(sv[4 * b + 2 * h], sv[4 * b + 2 * h + 1]), sl2_2, nmn2[h]);
+                        float2 e;
+                        if ((b & 3) == 3) {
+                            e = exp2_poly2(x);
+                        } else {
+                            e.x = ex2_approx(x.x);
+                            e.y = ex2_approx(x.y);
+                        }
+                        rs[h] = fadd2(rs[h], e);
+                        pk[2 * bb + h] = pack_h2(e.x, e.y);
                     }
-                    rs[h] = fadd2(rs[h], e);
-                    pk[2 * b + h] = pack_h2(e.x, e.y);
+                if (hb == 0 && j > 0) {
+                    // P.V of the previous tile must be complete: it reads the P columns and accumulates into O
+                    ok = __all_sync(0xffffffff,
+                                    mbar_wait_spin(&s.bar_od, (j - 1) & 1, abort, limit_ns, status, K_ENC, 31));
+                    if (!ok) break;
+                    tc_fence_after();
                 }
+                tmem_st_16x128b_x8(tl + (tP - tbase) + hb * 32, pk);
+            }
+            if (!ok) break;
 #pragma unroll
             for (int h = 0; h < 2; h++) l[h] = l[h] * corr[h] + (rs[h].x + rs[h].y);
-            if (j > 0) {
-                // P.V of the previous tile must be complete: it reads the P columns and accumulates into O
-                ok = __all_sync(0xffffffff, mbar_wait_spin(&s.bar_od, (j - 1) & 1, abort, limit_ns, status, K_ENC, 31));
-                if (!ok) break;
-                tc_fence_after();
-            }
-            tmem_st_16x128b_x16(tl + (tP - tbase), pk);
             // the running max moved: rescale the two O rows before the next P.V
             if (j > 0 && __any_sync(0xffffffff, corr[0] != 1.f || corr[1] != 1.f)) {
                 uint32_t r[32];
