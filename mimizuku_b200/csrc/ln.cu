@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(128) ln_kernel(__half2* x, const __half2* dd, 
 // runs the per-warp butterfly on each, and adds the four warp sums as (w0 + w2) + (w1 + w3): the reference's
 // arithmetic without a barrier or shared memory. Every load of the row is issued before the first store.
 template <int KP, bool ADD>
-__global__ void __launch_bounds__(128) ln_warp_kernel(__half2* x, const __half2* dd, const __half2* w,
+__global__ void __launch_bounds__(128, 8) ln_warp_kernel(__half2* x, const __half2* dd, const __half2* w,
                                                       const __half2* bias, __half2* out, int rows, int n2,
                                                       float eps) {
     griddep_wait();  // launched as a programmatic dependent: x and d come from the kernel before
