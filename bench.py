@@ -398,7 +398,7 @@ def main():
         "data": "synthetic (seeded 30 s clips: 1-8 sinusoids 80-4000 Hz + noise at 10 dB SNR; random-init weights)",
         "config": {"workload": "e2e whisper large-v3 (random init), 32 clips of 30 s per GPU, encoder groups of 8, "
                                "224 fixed greedy tokens (eos suppressed), 10 alignment heads, DTW timestamps",
-                   "clips_per_gpu": CLIPS_PER_GPU, "new_tokens": NEW_TOKENS,
+                   "clips_per_gpu": CLIPS_PER_GPU, "new_tokens": NEW_TOKENS, "decoder_lanes": e.lanes,
                    "l2": "inputs larger than L2: cross k/v 7.9 GB and weights 3.1 GB per GPU are streamed each step"},
         "e2e": {"value": round(e2e, 3), "unit": "clips/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),

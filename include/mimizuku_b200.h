@@ -196,6 +196,15 @@ int mmz_engine_step(mmz_engine* e, int b, int prompt_len);
 /* Captures Engine::step as a CUDA graph (src/transcribe.rs:122-131); mmz_engine_replay launches it once. */
 int mmz_engine_capture(mmz_engine* e, int b, int prompt_len);
 int mmz_engine_replay(mmz_engine* e);
+/* Decoder-step lanes (no counterpart in the reference, whose Rust host decodes on one stream): 1 runs every layer of
+ * the step for the whole batch on the engine's stream, as src/model.rs:648-736 does; 2 (the default of the native
+ * image) runs the layers of the two halves of a 32-sequence batch on two streams, forked after the embedding and
+ * joined before the logits, so that the launch- and latency-bound kernels of one half overlap the other half's. The
+ * step's kernels work sequence by sequence and cuBLAS returns the same rows for 16 sequences as for 32, so both
+ * settings give identical results; other batch sizes always decode on one lane. Engines on a fatbin image accept
+ * only 1. Takes effect at the next step or capture. */
+int mmz_engine_set_lanes(mmz_engine* e, int lanes);
+int mmz_engine_lanes(mmz_engine* e);
 /* Device address of an engine buffer: "tok", "done", "ctr", "align", "logits", "eh", "eqkv", "eatt", "xkv", "mel",
  * "kc", "vc", "x", "hb", "att", "aslot"; NULL if unknown. */
 void* mmz_engine_buffer(mmz_engine* e, const char* name);

@@ -83,6 +83,8 @@ SIGNATURES = {
     "mmz_engine_step": (_I, [_P, _I, _I]),
     "mmz_engine_capture": (_I, [_P, _I, _I]),
     "mmz_engine_replay": (_I, [_P]),
+    "mmz_engine_set_lanes": (_I, [_P, _I]),
+    "mmz_engine_lanes": (_I, [_P]),
     "mmz_engine_buffer": (_P, [_P, ctypes.c_char_p]),
     "mmz_engine_stream": (_P, [_P]),
     "mmz_engine_sync": (_I, [_P]),

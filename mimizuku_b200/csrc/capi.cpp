@@ -215,6 +215,8 @@ int mmz_engine_capture(mmz_engine* e, int b, int prompt_len) {
     return e ? e->e->capture(b, prompt_len) : fail("null engine");
 }
 int mmz_engine_replay(mmz_engine* e) { return e ? e->e->replay() : fail("null engine"); }
+int mmz_engine_set_lanes(mmz_engine* e, int lanes) { return e ? e->e->set_lanes(lanes) : fail("null engine"); }
+int mmz_engine_lanes(mmz_engine* e) { return e ? e->e->lanes() : 0; }
 void* mmz_engine_buffer(mmz_engine* e, const char* name) { return e && name ? e->e->buffer(name) : nullptr; }
 void* mmz_engine_stream(mmz_engine* e) { return e ? (void*)e->e->stream() : nullptr; }
 int mmz_engine_sync(mmz_engine* e) {

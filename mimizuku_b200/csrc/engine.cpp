@@ -21,6 +21,11 @@ constexpr int NFRAMES = 3000;
 constexpr int NCH = (TENC_ + 63) / 64;
 constexpr float EPS = 1e-5f;            // model.rs:12
 constexpr size_t WS_BYTES = 64u << 20;  // fixed cuBLAS workspace: no allocation during graph capture (gpu.rs:41)
+// Two decoder lanes split a batch of exactly 32 sequences into halves of 16: the one split for which cuBLAS's decoder
+// GEMMs (cublasGemmStridedBatchedEx, T/N, fp16, fp32 compute; every large-v3 and tiny shape) return the same rows for
+// 16 sequences as for 32. Smaller halves do not (4 + 5 of 9 and 12 + 12 of 24 differ in some shapes), so other batch
+// sizes decode on one lane.
+constexpr int LANE_ROWS = 16;
 
 // ============================================================================ kernel images
 
@@ -77,12 +82,16 @@ class NativeKernels : public Kernels {
         return ++launches, launch_self_attn(qkv, kc, vc, att, ctr, done, b, maxT, d, st);
     }
     // three kernels chained by programmatic dependent launches, on the engine's cross-attention scratch
-    int cross_attn(const void* xq, const void* kv, void*, void*, void*, void* att, void* align, const int* aslot,
+    // (s: where this call's scratch starts inside the engine's, so that two decoder lanes use disjoint parts)
+    int cross_attn(const void* xq, const void* kv, void* s, void*, void*, void* att, void* align, const int* aslot,
                    const int* ctr, const int* done, int b, int layer, int nl, int d, int, int na, int maxT,
                    cudaStream_t st) override {
+        char* base = s ? (char*)s : (char*)xscratch;
+        const size_t used = (size_t)(base - (char*)xscratch);
+        if (used > xscratch_bytes) return fail("cross_attn: scratch offset out of range");
         launches += 3;
-        return launch_cross_attn(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, xscratch,
-                                 xscratch_bytes, st);
+        return launch_cross_attn(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, base,
+                                 xscratch_bytes - used, st);
     }
     int embed(const int* tok, const int* ctr, const void* emb, const void* dpos, void* x, int b, int maxT, int d,
               cudaStream_t st) override {
@@ -371,6 +380,18 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         err_ = "cuBLAS workspace";
         return;
     }
+    if (k_->native()) {  // the second decoder lane: its own stream, cuBLAS handle and workspace
+        ws2_ = alloc(WS_BYTES);
+        if (!ws2_ || cudaStreamCreateWithFlags(&st2_, cudaStreamNonBlocking) != cudaSuccess ||
+            cublasCreate(&blas2_) != CUBLAS_STATUS_SUCCESS || cublasSetStream(blas2_, st2_) != CUBLAS_STATUS_SUCCESS ||
+            cublasSetWorkspace(blas2_, ws2_, WS_BYTES) != CUBLAS_STATUS_SUCCESS ||
+            cudaEventCreateWithFlags(&fork_ev_, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&join_ev_, cudaEventDisableTiming) != cudaSuccess) {
+            err_ = "second decoder lane setup failed";
+            return;
+        }
+        lanes_ = 2;
+    }
     const int na = (int)gc_.align_heads.size();
     auto H = [&](size_t n) { return alloc(n * 2); };
     const size_t r1 = (size_t)eg * NFRAMES, r2 = (size_t)eg * TENC_;
@@ -463,8 +484,13 @@ Engine::~Engine() {
     if (st_) cudaStreamSynchronize(st_);
     k_.reset();
     for (void* p : allocs_) cudaFree(p);
+    if (st2_) cudaStreamSynchronize(st2_);
     if (blas_) cublasDestroy(blas_);
+    if (blas2_) cublasDestroy(blas2_);
     if (lt_) cublasLtDestroy(lt_);
+    if (fork_ev_) cudaEventDestroy(fork_ev_);
+    if (join_ev_) cudaEventDestroy(join_ev_);
+    if (st2_) cudaStreamDestroy(st2_);
     if (poll_ev_) cudaEventDestroy(poll_ev_);
     if (done_host_) cudaFreeHost(done_host_);
     if (st_) cudaStreamDestroy(st_);
@@ -528,9 +554,10 @@ void* Engine::dec_out(int i, int which) const {
 
 // column-major strided-batched fp16 GEMM, fp32 accumulation (gpu.rs:254-286)
 int Engine::matmul(bool ta, bool tb, int m, int n, int k, float alpha, const void* a, int lda, long long sa,
-                   const void* b, int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch) {
+                   const void* b, int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch,
+                   cublasHandle_t h) {
     cublasStatus_t r = cublasGemmStridedBatchedEx(
-        blas_, ta ? CUBLAS_OP_T : CUBLAS_OP_N, tb ? CUBLAS_OP_T : CUBLAS_OP_N, m, n, k, &alpha, a, CUDA_R_16F, lda, sa,
+        h ? h : blas_, ta ? CUBLAS_OP_T : CUBLAS_OP_N, tb ? CUBLAS_OP_T : CUBLAS_OP_N, m, n, k, &alpha, a, CUDA_R_16F, lda, sa,
         b, CUDA_R_16F, ldb, sb, &beta, c, CUDA_R_16F, ldc, sc, batch, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
     return r == CUBLAS_STATUS_SUCCESS ? 0 : failf("cublasGemmStridedBatchedEx failed (%d)", (int)r);
 }
@@ -548,11 +575,16 @@ int Engine::lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, i
 
 // the same for a y that already holds the bias (gpu.rs:238-247)
 int Engine::lin_onto_bias(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k) {
+    return lin_onto_bias_on(x, ldx, l, y, ldy, m, n, k, st_, blas_);
+}
+
+int Engine::lin_onto_bias_on(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k,
+                             cudaStream_t st, cublasHandle_t h) {
     if (m <= 8) {
-        int r = k_->gemv(x, ldx, l.w, y, ldy, m, n, k, l.b, st_);
+        int r = k_->gemv(x, ldx, l.w, y, ldy, m, n, k, l.b, st);
         if (r != -2) return r;
     }
-    return matmul(true, false, n, m, k, 1.f, l.w, k, 0, x, ldx, 0, 1.f, y, ldy, 0, 1);
+    return matmul(true, false, n, m, k, 1.f, l.w, k, 0, x, ldx, 0, 1.f, y, ldy, 0, 1, h);
 }
 
 // The native encoder's linear layers take their bias in the GEMM's epilogue instead of a bias image that the GEMM
@@ -683,32 +715,71 @@ int Engine::reset(const int* prompts, int b, int np) {
     return 0;
 }
 
-// model.rs:648-736
-int Engine::step(int b, int prompt_len) {
+int Engine::set_lanes(int n) {
+    if (n != 1 && n != 2) return fail("set_lanes: 1 or 2");
+    if (n == 2 && !st2_) return fail("set_lanes: the fatbin image decodes on one lane");
+    lanes_ = n;
+    return 0;
+}
+
+// model.rs:665-705 for the sequences [r0, r0 + bh): every buffer of the step is [sequence][...], so a lane works on
+// its rows of each (and on its own part of the cross-attention scratch)
+int Engine::dec_layer(int i, int r0, int bh, cudaStream_t st, cublasHandle_t h) {
     const int d = dm_.d, ff = dm_.ff, nh = dm_.nh, nl = dm_.dec_layers, mt = dm_.max_t;
     const int na = (int)gc_.align_heads.size();
+    const DecLayer& l = dec_[i];
+    auto rows = [&](void* p, size_t n) { return (void*)((char*)p + 2 * (size_t)r0 * n); };  // row r0 of fp16 [.][n]
+    void* kc = (char*)kc_ + 2 * ((size_t)i * bmax_ + r0) * mt * d;
+    void* vc = (char*)vc_ + 2 * ((size_t)i * bmax_ + r0) * mt * d;
+    void *oqkv = rows(dec_out(i, 0), 3 * d), *oo = rows(dec_out(i, 1), d), *oxq = rows(dec_out(i, 2), d),
+         *oxo = rows(dec_out(i, 3), d), *ofc1 = rows(dec_out(i, 4), ff), *ofc2 = rows(dec_out(i, 5), d);
+    void *x = rows(x_, d), *hb = rows(hb_, d), *att = rows(att_, d);
+    const int* done = done_ + r0;
+    const void* xkv = (const char*)xkv_buf_ + 2 * (size_t)r0 * nl * 2 * d * TENC_;
+    void* align = (char*)align_ + 2 * (size_t)r0 * mt * na * TENC_;
+    void* xs = s_;
+    if (r0 > 0) {
+        if (!k_->native()) return fail("dec_layer: the fatbin image decodes the whole batch on one lane");
+        xs = (char*)s_ + cross_attn_scratch_bytes(r0, d);
+    }
+    CK(lin_onto_bias_on(hb, d, l.qkv, oqkv, 3 * d, bh, 3 * d, d, st, h));
+    CK(k_->self_attn(oqkv, kc, vc, att, ctr_, done, bh, mt, d, nh, st));
+    CK(lin_onto_bias_on(att, d, l.o, oo, d, bh, d, d, st, h));
+    CK(k_->add_layernorm(x, oo, l.lnx, hb, bh, d, st));
+    CK(lin_onto_bias_on(hb, d, l.xq, oxq, d, bh, d, d, st, h));
+    CK(k_->cross_attn(oxq, xkv, xs, stat_, part_, att, align, aslot_, ctr_, done, bh, i, nl, d, nh, na, mt, st));
+    CK(lin_onto_bias_on(att, d, l.xo, oxo, d, bh, d, d, st, h));
+    CK(k_->add_layernorm(x, oxo, l.ln3, hb, bh, d, st));
+    CK(lin_onto_bias_on(hb, d, l.fc1, ofc1, ff, bh, ff, d, st, h));
+    CK(k_->gelu(ofc1, (long)bh * ff, st));
+    CK(lin_onto_bias_on(ofc1, ff, l.fc2, ofc2, d, bh, d, ff, st, h));
+    const Ln& next = i + 1 < nl ? dec_[i + 1].ln1 : dln_;
+    return k_->add_layernorm(x, ofc2, next, hb, bh, d, st);
+}
+
+// model.rs:648-736
+int Engine::step(int b, int prompt_len) {
+    const int d = dm_.d, ff = dm_.ff, nl = dm_.dec_layers, mt = dm_.max_t;
     CK(k_->embed(tok_, ctr_, emb_, dpos_, x_, b, mt, d, st_));
     CK(k_->layernorm(x_, dec_[0].ln1, hb_, b, d, st_));
     CUDA_CK(cudaMemcpyAsync(dout_, dbias_, (size_t)2 * nl * bmax_ * (7 * d + ff), cudaMemcpyDeviceToDevice, st_));
-    for (int i = 0; i < nl; i++) {
-        const DecLayer& l = dec_[i];
-        void* kc = (char*)kc_ + 2 * (size_t)i * bmax_ * mt * d;
-        void* vc = (char*)vc_ + 2 * (size_t)i * bmax_ * mt * d;
-        void *oqkv = dec_out(i, 0), *oo = dec_out(i, 1), *oxq = dec_out(i, 2), *oxo = dec_out(i, 3),
-             *ofc1 = dec_out(i, 4), *ofc2 = dec_out(i, 5);
-        CK(lin_onto_bias(hb_, d, l.qkv, oqkv, 3 * d, b, 3 * d, d));
-        CK(k_->self_attn(oqkv, kc, vc, att_, ctr_, done_, b, mt, d, nh, st_));
-        CK(lin_onto_bias(att_, d, l.o, oo, d, b, d, d));
-        CK(k_->add_layernorm(x_, oo, l.lnx, hb_, b, d, st_));
-        CK(lin_onto_bias(hb_, d, l.xq, oxq, d, b, d, d));
-        CK(k_->cross_attn(oxq, xkv_buf_, s_, stat_, part_, att_, align_, aslot_, ctr_, done_, b, i, nl, d, nh, na, mt, st_));
-        CK(lin_onto_bias(att_, d, l.xo, oxo, d, b, d, d));
-        CK(k_->add_layernorm(x_, oxo, l.ln3, hb_, b, d, st_));
-        CK(lin_onto_bias(hb_, d, l.fc1, ofc1, ff, b, ff, d));
-        CK(k_->gelu(ofc1, (long)b * ff, st_));
-        CK(lin_onto_bias(ofc1, ff, l.fc2, ofc2, d, b, d, ff));
-        const Ln& next = i + 1 < nl ? dec_[i + 1].ln1 : dln_;
-        CK(k_->add_layernorm(x_, ofc2, next, hb_, b, d, st_));
+    if (lanes_ == 2 && b == 2 * LANE_ROWS) {
+        // two lanes: the first half of the sequences on the engine's stream, the second half on the other; forked
+        // here, joined before the logits (also inside a graph capture, where the second stream joins the capture)
+        const int b0 = LANE_ROWS;
+        CUDA_CK(cudaEventRecord(fork_ev_, st_));
+        CUDA_CK(cudaStreamWaitEvent(st2_, fork_ev_, 0));
+        int r = 0;
+        for (int i = 0; i < nl && !r; i++) {
+            r = dec_layer(i, 0, b0, st_, blas_);
+            if (!r) r = dec_layer(i, b0, b - b0, st2_, blas2_);
+        }
+        // the join is recorded even after a failure, so that a capture in progress ends with both streams joined
+        CUDA_CK(cudaEventRecord(join_ev_, st2_));
+        CUDA_CK(cudaStreamWaitEvent(st_, join_ev_, 0));
+        if (r) return -1;
+    } else {
+        for (int i = 0; i < nl; i++) CK(dec_layer(i, 0, b, st_, blas_));
     }
     // logits = hb emb^T (no bias), then the greedy choice and the position counter
     const int lr = k_->logits(hb_, d, emb_, logits_, dm_.vocab, b, d, st_);

@@ -83,6 +83,14 @@ class Engine {
     long long launches() const;
     long long step_launches() const { return step_launches_; }
     size_t last_d2h_bytes() const { return d2h_bytes_; }
+    // decoder-step lanes: 1 runs the step's layers for the whole batch on one stream, as src/model.rs does; 2 (the
+    // native image's default) splits a batch of 32 into two halves whose layers run on two streams (one cuBLAS handle
+    // and workspace each), forked after the embedding and joined before the logits, so that the latency-bound
+    // launches of one half overlap the other's. Every kernel of the step works row by row and cuBLAS gives the same
+    // rows for 16 sequences as for 32, so both settings give the same results; other batch sizes use one lane. The
+    // fatbin image always uses 1.
+    int set_lanes(int n);
+    int lanes() const { return lanes_; }
 
    private:
     int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
@@ -93,7 +101,13 @@ class Engine {
                   long long sy, int m, int n, int k, int batch);
     int lin_enc(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
     int matmul(bool ta, bool tb, int m, int n, int k, float alpha, const void* a, int lda, long long sa, const void* b,
-               int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch);
+               int ldb, long long sb, float beta, void* c, int ldc, long long sc, int batch,
+               cublasHandle_t h = nullptr);
+    // lin_onto_bias on a given stream and cuBLAS handle (one decoder lane)
+    int lin_onto_bias_on(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k, cudaStream_t st,
+                         cublasHandle_t h);
+    // decoder layer i (model.rs:665-705) for the sequences [r0, r0 + bh) on stream st with cuBLAS handle h
+    int dec_layer(int i, int r0, int bh, cudaStream_t st, cublasHandle_t h);
     void* alloc(size_t bytes);
     int decode_and_times(const int* frames, int n, const int* prompt, int np, int max_steps, bool graph, int threads,
                          int* tokens, int* lens, float* times, double* stage_s,
@@ -108,6 +122,11 @@ class Engine {
     int dev_ = 0;
     cudaStream_t st_ = nullptr;
     cublasHandle_t blas_ = nullptr;
+    int lanes_ = 1;
+    cudaStream_t st2_ = nullptr;     // second decoder lane
+    cublasHandle_t blas2_ = nullptr;
+    void* ws2_ = nullptr;
+    cudaEvent_t fork_ev_ = nullptr, join_ev_ = nullptr;
     cublasLtHandle_t lt_ = nullptr;
     struct LtPlan {
         long long key[8];

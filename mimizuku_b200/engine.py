@@ -46,11 +46,13 @@ def align_heads(cfg: ModelConfig, n: Optional[int] = None, seed: int = 0):
 class Engine:
     """Engine::new (src/model.rs:333-514) with seeded random-init weights. kernel_image=None runs the sm_100a kernels
     of this library; a path runs a fatbin exporting the reference's kernel names (e.g. the reference's own
-    kernels/whisper.cu build) through the same host code."""
+    kernels/whisper.cu build) through the same host code. lanes: decoder-step lanes (None: the image's default, 2 for
+    the native kernels, 1 for a fatbin)."""
 
     def __init__(self, cfg: ModelConfig, bmax: int, eg: int = 8, device: int = 0, kernel_image: Optional[str] = None,
                  seed: int = 0, heads: Optional[Sequence[Tuple[int, int]]] = None,
-                 suppress: Optional[Sequence[int]] = None, begin_suppress: Optional[Tuple[int, int]] = None):
+                 suppress: Optional[Sequence[int]] = None, begin_suppress: Optional[Tuple[int, int]] = None,
+                 lanes: Optional[int] = None):
         self.cfg = cfg
         self.bmax, self.eg, self.device = bmax, min(eg, bmax), device
         self.heads = list(heads) if heads is not None else align_heads(cfg)
@@ -66,6 +68,8 @@ class Engine:
         self._h = lib.mmz_engine_create(ctypes.byref(dims), ctypes.byref(gc), bmax, self.eg, device, img, seed)
         if not self._h:
             raise MmzError(lib.mmz_last_error().decode())
+        if lanes is not None:
+            self.lanes = lanes
 
     @property
     def na(self):
@@ -143,6 +147,17 @@ class Engine:
 
     def replay(self):
         _check(lib.mmz_engine_replay(self._h), "replay")
+
+    @property
+    def lanes(self):
+        """Decoder-step lanes: 1 decodes the whole batch on one stream (the reference's way), 2 (the native image's
+        default) the two halves of a 32-sequence batch on two concurrent streams (other batch sizes use one lane);
+        results are the same."""
+        return lib.mmz_engine_lanes(self._h)
+
+    @lanes.setter
+    def lanes(self, n):
+        _check(lib.mmz_engine_set_lanes(self._h, int(n)), "set_lanes")
 
     def buffer(self, name):
         p = lib.mmz_engine_buffer(self._h, name.encode())

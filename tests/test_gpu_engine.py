@@ -203,3 +203,38 @@ def test_transcribe_from_audio_is_transcribe_of_the_gpu_features(cuda):
     for k in ("tokens", "lens", "times"):
         assert np.array_equal(r[k], x[k]), k
     e.close()
+
+
+@pytest.mark.parametrize("name,b,new", [("TINY", 32, 24), ("TINY", 9, 24), ("LARGE_V3_TURBO", 32, 12)])
+def test_two_decoder_lanes_match_one(cuda, name, b, new):
+    """Two decoder lanes (the halves of a 32-sequence batch on two streams, the native image's default) give exactly
+    the tokens, alignment rows and token times of one lane (the whole batch on one stream, as src/model.rs runs the
+    step), in the captured graph and eagerly; the turbo case has large-v3's decoder GEMM shapes. A batch of 9 decodes
+    on one lane whatever the setting."""
+    import mimizuku_b200 as m
+    cfg = getattr(m, name)
+    mel, frames = _clips(b, cfg.n_mels, seed=2)
+    e = m.Engine(cfg, bmax=b, eg=8, seed=5, suppress=[cfg.eos])
+    assert e.lanes == 2
+    out = {}
+    for lanes in (2, 1):
+        e.lanes = lanes
+        for graph in (True, False):
+            r = e.transcribe(mel, frames, max_new=new, graph=graph)
+            r["align"] = _align_rows(e, cfg, b)
+            out[lanes, graph] = r
+    for k in ("tokens", "lens", "times", "align"):
+        for key in out:
+            assert np.array_equal(out[key][k], out[1, True][k]), (key, k)
+    assert (out[2, True]["lens"] == len(cfg.prompt) + new).all()
+    e.close()
+
+
+def test_fatbin_engine_decodes_on_one_lane(cuda, ref):
+    """An engine on the reference's kernels keeps the reference host's single stream and refuses a second lane."""
+    import mimizuku_b200 as m
+    e = m.Engine(m.TINY, bmax=2, eg=2, kernel_image=O.REF_FATBIN)
+    assert e.lanes == 1
+    with pytest.raises(m.MmzError):
+        e.lanes = 2
+    e.close()
