@@ -2,7 +2,8 @@
 // position folded in) and cross-attention over the 1500 encoder positions, which also records the alignment-head
 // probabilities. Both are memory-bound:
 //   self-attention   one CTA per (sequence, head) streams its K then V rows through an 8-deep ring of TMA tensor
-//                    copies; the reference's thread mapping makes every sum run in the reference's order
+//                    copies; one key per thread for the scores (the reference's warp butterfly restated as a tree),
+//                    the reference's thread mapping for the softmax and P.V, so every sum runs in the reference's order
 //   cross-attention  split-KV over 8 slices of 192 positions per (sequence, head), as two streaming kernels with
 //                    every 16-byte load of a thread in flight at once and a small combine, chained by programmatic
 //                    dependent launches
@@ -41,13 +42,14 @@ constexpr int SSTAGE = 8;   // copies in flight per CTA
 constexpr int SMAXL = 512;  // longest context (max_t)
 
 struct SelfSmem {
-    h16 ring[SSTAGE][STILE * HD];  // 8 x 4 KB: K tiles, then V tiles, streamed through
+    h16 ring[SSTAGE][STILE * HD];  // 8 x 4 KB: K tiles (128-byte swizzle), then V tiles (plain), streamed through
     float q[HD];
     float sc[SMAXL];               // scores, then probabilities
     float wmax[4], wsum[4];        // per-warp partials of the block max and the block sum
     float red[HD];
     uint64_t full[SSTAGE];
     int abort;
+    int nissued;                   // tiles issued so far (the highest index + 1)
 };
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -64,10 +66,46 @@ __device__ __forceinline__ void row_copy8(h16* dst, const h16* src, int t8) {
     reinterpret_cast<uint4*>(dst)[t8] = reinterpret_cast<const uint4*>(src)[t8];
 }
 
-// grid (heads, B), block 128: one CTA per (sequence, head), the reference's thread mapping (kernels/whisper.cu:321-353)
-// so that every sum runs in the reference's order, with the L = ctr[0] + 1 cached rows streamed through an 8-deep ring
-// of 32-row tensor copies (kmap / vmap: 2-D maps over this layer's caches [B * maxT rows][d], box 64 x 32): the K
-// tiles, then the V tiles. 640 CTAs of 34 KB fit on the GPU at once, so the whole launch is one wave.
+// One key's score by one thread, bit for bit the reference's warp computation (kernels/whisper.cu:331-336): lane l's
+// product q[2l] k[2l] + q[2l+1] k[2l+1] (contracted as fma(q[2l], k[2l], q[2l+1] k[2l+1])) and the xor-butterfly
+// over 16, 8, 4, 2, 1, after which every lane holds the same sum, whose association is this tree:
+// v1[i] = a[i] + a[i+16], v2[i] = v1[i] + v1[i+8], v3[i] = v2[i] + v2[i+4], (v3[0] + v3[2]) + (v3[1] + v3[3]).
+// k: the key's 64 halves as eight 16-byte chunks (chunk c holds lanes 4c .. 4c + 3).
+__device__ __forceinline__ float self_score(const float* __restrict__ q, const uint4 (&k)[8]) {
+    float a[32];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&k[c]);
+        const float4 qa = reinterpret_cast<const float4*>(q)[2 * c];
+        const float4 qb = reinterpret_cast<const float4*>(q)[2 * c + 1];
+        const float qq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float2 k2 = __half22float2(h2[e]);
+            a[4 * c + e] = __fmaf_rn(qq[2 * e], k2.x, __fmul_rn(qq[2 * e + 1], k2.y));
+        }
+    }
+    float v1[16], v2[8], v3[4];
+#pragma unroll
+    for (int i = 0; i < 16; i++) v1[i] = __fadd_rn(a[i], a[i + 16]);
+#pragma unroll
+    for (int i = 0; i < 8; i++) v2[i] = __fadd_rn(v1[i], v1[i + 8]);
+#pragma unroll
+    for (int i = 0; i < 4; i++) v3[i] = __fadd_rn(v2[i], v2[i + 4]);
+    return __fadd_rn(__fadd_rn(v3[0], v3[2]), __fadd_rn(v3[1], v3[3]));
+}
+
+// grid (heads, B), block 128: one CTA per (sequence, head) (kernels/whisper.cu:321-353). The L = ctr[0] + 1 cached
+// rows stream through an 8-deep ring of 32-row tensor copies (kmap: 128-byte swizzle, vmap: plain; 2-D maps over this
+// layer's caches [B * maxT rows][d], box 64 x 32): the K tiles, then the V tiles.
+//   scores   warp w takes the K tiles w, w + 4, ...: one key per lane, the whole 64-term product and the reference's
+//            butterfly association in registers (self_score); the warp refills the stage it read by itself
+//   softmax  the reference's block max and block sum (thread t sums the positions t, t + 128, ... in order)
+//   P.V      thread (half, column) runs through the positions of its parity in order (:346-349), with each tile's
+//            16 probabilities and values loaded before the chain of fused multiply-adds
+// ctr[0], done and the cache rows before ctr[0] are read before the wait for the kernel before (they come from earlier
+// decoding steps), so the first copies overlap that kernel's tail; row ctr[0] comes from qkv after the wait.
+// 640 CTAs of 35 KB fit on the GPU at once, so the whole launch is one wave.
 __global__ void __launch_bounds__(128)
     self_attn_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                      const h16* __restrict__ qkv, h16* __restrict__ kc, h16* __restrict__ vc, h16* __restrict__ out,
@@ -75,89 +113,116 @@ __global__ void __launch_bounds__(128)
                      unsigned long long limit_ns) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     SelfSmem& s = *reinterpret_cast<SelfSmem*>(smem_raw);
-    griddep_wait();  // launched as a programmatic dependent of the qkv projection
     const int hh = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
     const int w = t >> 5, lane = t & 31;
-    const int p = ctr[0], L = p + 1;
-    const long qrow = (long)b * 3 * d;
-    const long crow = ((long)b * maxT + p) * d + hh * HD;
-    if (t < 8) {  // the cache row of position p, for every sequence (kernels/whisper.cu:310-317)
-        row_copy8(kc + crow, qkv + qrow + d + hh * HD, t);
-        row_copy8(vc + crow, qkv + qrow + 2 * d + hh * HD, t);
+    if (smem_u32(smem_raw) & 1023) {  // the swizzled K tiles need a 1024-byte aligned ring
+        if (t == 0) report(status, ST_MISALIGNED, K_SELF, 0);
+        return;
     }
-    if (done[b]) return;
+    const int p = ctr[0], L = p + 1;
+    const bool live = done[b] == 0;
     const int ntile = (L + STILE - 1) / STILE, total = 2 * ntile;
     auto issue = [&](int i) {  // tile i: K rows [32 i, 32 i + 32) for i < ntile, else V rows of tile i - ntile
         const int st = i % SSTAGE;
         const int row0 = b * maxT + (i < ntile ? i : i - ntile) * STILE;
         mbar_expect_tx(&s.full[st], STILE * HD * 2);
         tma_load_2d(s.ring[st], i < ntile ? &kmap : &vmap, hh * HD, row0, &s.full[st]);
+        atomicMax(&s.nissued, i + 1);
     };
-    if (t == 0) {
+    if (t == 0 && live) {
         s.abort = 0;
+        s.nissued = 0;
         for (int i = 0; i < SSTAGE; i++) mbar_init(&s.full[i], 1);
         fence_mbar_init();
         for (int i = 0; i < SSTAGE && i < total; i++) issue(i);
     }
+    griddep_wait();  // launched as a programmatic dependent of the qkv projection
+    const long qrow = (long)b * 3 * d;
+    const long crow = ((long)b * maxT + p) * d + hh * HD;
+    if (t < 8) {  // the cache row of position p, for every sequence (kernels/whisper.cu:310-317)
+        row_copy8(kc + crow, qkv + qrow + d + hh * HD, t);
+        row_copy8(vc + crow, qkv + qrow + 2 * d + hh * HD, t);
+    }
+    if (!live) return;
     if (t < HD) s.q[t] = rh(f(qkv[qrow + hh * HD + t]) * 0.125f);  // :327
     __syncthreads();
-    const int col = t & (HD - 1), half = t >> 6;
-    float acc = 0.f, m = 0.f, sum = 0.f;
-    for (int i = 0; i < total; i++) {
+
+    // ---------------------------------------------------------------- scores (:329-337)
+    for (int i = w; i < ntile; i += 4) {
         const int st = i % SSTAGE;
-        const bool is_k = i < ntile;
-        const int j0 = (is_k ? i : i - ntile) * STILE;
-        mbar_wait_spin(&s.full[st], (i / SSTAGE) & 1, &s.abort, limit_ns, status, K_SELF, 1);
+        if (!__all_sync(0xffffffff, mbar_wait_spin(&s.full[st], (i / SSTAGE) & 1, &s.abort, limit_ns, status,
+                                                    K_SELF, 1)))
+            break;
+        const int j = i * STILE + lane;
+        if (j < L) {
+            uint4 k[8];
+            if (j == p) {  // the current position's key comes from qkv (its cache row is written above)
+                const uint4* src = reinterpret_cast<const uint4*>(qkv + qrow + d + hh * HD);
+#pragma unroll
+                for (int c = 0; c < 8; c++) k[c] = src[c];
+            } else {
+                const unsigned char* row = reinterpret_cast<const unsigned char*>(s.ring[st]) + lane * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++) k[c] = *reinterpret_cast<const uint4*>(row + ((c ^ (lane & 7)) << 4));
+            }
+            s.sc[j] = rh(self_score(s.q, k));  // :335
+        }
+        __syncwarp();
+        if (lane == 0 && i + SSTAGE < total) issue(i + SSTAGE);  // only this warp read the stage
+    }
+    __syncthreads();
+
+    // ---------------------------------------------------------------- softmax (:338-344, block_max / block_sum :22-46)
+    // (the butterfly over the four warp values is their max, and (w0 + w2) + (w1 + w3) for the sum)
+    float mx = -INFINITY;
+    for (int j = t; j < L; j += 128) mx = fmaxf(mx, s.sc[j]);
+    mx = warp_max(mx);
+    if (lane == 0) s.wmax[w] = mx;
+    __syncthreads();
+    const float m = fmaxf(fmaxf(s.wmax[0], s.wmax[1]), fmaxf(s.wmax[2], s.wmax[3]));
+    float ex[SMAXL / 128];
+    float e = 0.f;
+#pragma unroll
+    for (int u = 0; u < SMAXL / 128; u++) {
+        const int j = t + 128 * u;
+        ex[u] = j < L ? expf(s.sc[j] - m) : 0.f;
+        if (j < L) e += ex[u];
+    }
+    e = warp_sum(e);
+    if (lane == 0) s.wsum[w] = e;
+    __syncthreads();
+    const float sum = (s.wsum[0] + s.wsum[2]) + (s.wsum[1] + s.wsum[3]);
+#pragma unroll
+    for (int u = 0; u < SMAXL / 128; u++)
+        if (t + 128 * u < L) s.sc[t + 128 * u] = rh(ex[u] / sum);
+    __syncthreads();
+
+    // ---------------------------------------------------------------- P.V (:345-352)
+    const int col = t & (HD - 1), half = t >> 6;
+    float acc = 0.f;
+    for (int v = 0; v < ntile; v++) {
+        const int i = ntile + v, st = i % SSTAGE, j0 = v * STILE;
+        mbar_wait_spin(&s.full[st], (i / SSTAGE) & 1, &s.abort, limit_ns, status, K_SELF, 2);
         h16* tile = s.ring[st];
-        if (p >= j0 && p < j0 + STILE) {  // the current position comes from qkv (its cache row is written above)
-            if (t < 8) row_copy8(tile + (p - j0) * HD, qkv + qrow + (is_k ? d : 2 * d) + hh * HD, t);
+        if (p >= j0 && p < j0 + STILE) {  // the current position's values come from qkv
+            if (t < 8) row_copy8(tile + (p - j0) * HD, qkv + qrow + 2 * d + hh * HD, t);
             __syncthreads();
         }
-        if (is_k) {
-            // scores: a warp per position, 2 elements per lane (:331-336); the warp's 8 positions of the tile go
-            // through the butterfly together (independent chains, each in the reference's order)
-            float a[STILE / 4];
+        float pj[STILE / 2], vj[STILE / 2];
 #pragma unroll
-            for (int u = 0; u < STILE / 4; u++) {
-                const float2 k2 = __half22float2(reinterpret_cast<const __half2*>(tile + (w + 4 * u) * HD)[lane]);
-                a[u] = s.q[2 * lane] * k2.x + s.q[2 * lane + 1] * k2.y;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int u = 0; u < STILE / 4; u++) a[u] += __shfl_xor_sync(0xffffffff, a[u], o);
-            if (lane == 0)
-#pragma unroll
-                for (int u = 0; u < STILE / 4; u++)
-                    if (j0 + w + 4 * u < L) s.sc[j0 + w + 4 * u] = rh(a[u]);
-        } else {
-            if (i == ntile) {
-                // every score is in: the reference's block max and block sum (:338-344, block_max / block_sum :22-46)
-                // (the butterfly over the four warp values is their max, and (w0 + w2) + (w1 + w3) for the sum)
-                __syncthreads();
-                float mx = -INFINITY;
-                for (int j = t; j < L; j += 128) mx = fmaxf(mx, s.sc[j]);
-                mx = warp_max(mx);
-                if (lane == 0) s.wmax[w] = mx;
-                __syncthreads();
-                m = fmaxf(fmaxf(s.wmax[0], s.wmax[1]), fmaxf(s.wmax[2], s.wmax[3]));
-                float e = 0.f;
-                for (int j = t; j < L; j += 128) e += expf(s.sc[j] - m);
-                e = warp_sum(e);
-                if (lane == 0) s.wsum[w] = e;
-                __syncthreads();
-                sum = (s.wsum[0] + s.wsum[2]) + (s.wsum[1] + s.wsum[3]);
-                for (int j = t; j < L; j += 128) s.sc[j] = rh(expf(s.sc[j] - m) / sum);
-                __syncthreads();
-            }
-            // P.V: thread (half, column) runs through the positions of its parity in order (:346-349); tiles start
-            // at even positions
-            for (int jj = half; jj < STILE && j0 + jj < L; jj += 2)
-                acc += s.sc[j0 + jj] * f(tile[jj * HD + col]);
+        for (int u = 0; u < STILE / 2; u++) {  // tiles start at even positions: this thread's parity is half
+            pj[u] = s.sc[j0 + half + 2 * u];
+            vj[u] = f(tile[(half + 2 * u) * HD + col]);
         }
+#pragma unroll
+        for (int u = 0; u < STILE / 2; u++)
+            if (j0 + half + 2 * u < L) acc = __fmaf_rn(pj[u], vj[u], acc);
         if (i + SSTAGE < total) {  // the stage is refilled: everyone must be done with it
             __syncthreads();
-            if (t == 0) issue(i + SSTAGE);
+            if (t == 0) {
+                fence_proxy_async_smem();  // the stage may hold the row written above
+                issue(i + SSTAGE);
+            }
         }
     }
     // :350-352
@@ -165,7 +230,8 @@ __global__ void __launch_bounds__(128)
     __syncthreads();
     if (half == 0) out[(long)b * d + hh * HD + col] = h(acc + s.red[col]);
     if (t == 0 && s.abort) {  // a wait gave up: let the copies in flight land before the shared memory is released
-        for (int i = total - SSTAGE > 0 ? total - SSTAGE : 0; i < total; i++)
+        const int n = s.nissued;
+        for (int i = n - SSTAGE > 0 ? n - SSTAGE : 0; i < n; i++)
             mbar_wait(&s.full[i % SSTAGE], (i / SSTAGE) & 1, nullptr, limit_ns, nullptr, 0, 0);
     }
 }
@@ -439,7 +505,7 @@ int launch_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* 
     const uint64_t dims[2] = {(uint64_t)d, (uint64_t)batch * maxT};
     const uint64_t strides[1] = {(uint64_t)d * 2};
     const uint32_t box[2] = {HD, STILE};
-    if (make_tmap_2d(&km, kc, dims, strides, box, false) || make_tmap_2d(&vm, vc, dims, strides, box, false))
+    if (make_tmap_2d(&km, kc, dims, strides, box, true) || make_tmap_2d(&vm, vc, dims, strides, box, false))
         return fail("self_attn: cuTensorMapEncodeTiled failed");
     dim3 grid(d / HD, batch);
     return check_pdl(launch_pdl(self_attn_kernel, grid, dim3(128), sizeof(SelfSmem), st, km, vm, (const h16*)qkv,

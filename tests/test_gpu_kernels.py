@@ -199,6 +199,8 @@ def test_self_attn(cuda, ref, B, d, p):
     assert np.array_equal(host(VC).view(np.uint16), host(VCr).view(np.uint16))
     live = done == 0
     out, outr = f16(OUT), f16(OUTr)
+    # every sum runs in the reference's order: the outputs are the reference kernel's bit for bit
+    assert np.array_equal(host(OUT).view(np.uint16)[live], host(OUTr).view(np.uint16)[live])
     exact = O.self_attn_f64(qkv, kc, vc, p, done, max_t, d)
     err = np.abs(out[live] - exact[live]).max()
     err_r = np.abs(outr[live] - exact[live]).max()
