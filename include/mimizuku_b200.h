@@ -56,7 +56,10 @@ int mmz_enc_flash(const void* qkv, void* out, int groups, int d, void* stream);
 /* Causal decoder self-attention at position p = ctr[0] over the per-layer caches kc, vc [batch][max_t][d], with the
  * cache write of position p folded in: k and v of p are read from qkv [batch][3d] and stored into the caches.
  * Sequences with done[b] != 0 only get the cache write. out [batch][d]. Replaces kv_write + self_attn
- * (kernels/whisper.cu:310, :321; src/model.rs:665-672). max_t <= 512. */
+ * (kernels/whisper.cu:310, :321; src/model.rs:665-672). max_t <= 512. Outputs equal the reference kernel's bit for
+ * bit. Launched as a programmatic dependent of the kernel before it on the stream: ctr, done and the cache rows
+ * before ctr[0] are read before that kernel has finished (in the reference's decoding step they come from earlier
+ * steps), so they must not be written by the kernel immediately before this call; qkv may be. */
 int mmz_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* ctr, const int* done, int batch,
                   int max_t, int d, void* stream);
 
