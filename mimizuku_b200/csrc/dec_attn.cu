@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(128)
     __syncthreads();
 
     // ---------------------------------------------------------------- scores (:329-337)
+    float kmax = -INFINITY;  // this lane's largest score (the block max is exact in any order)
     for (int i = w; i < ntile; i += 4) {
         const int st = i % SSTAGE;
         if (!__all_sync(0xffffffff, mbar_wait_spin(&s.full[st], (i / SSTAGE) & 1, &s.abort, limit_ns, status,
@@ -165,20 +166,20 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
                 for (int c = 0; c < 8; c++) k[c] = *reinterpret_cast<const uint4*>(row + ((c ^ (lane & 7)) << 4));
             }
-            s.sc[j] = rh(self_score(s.q, k));  // :335
+            const float sj = rh(self_score(s.q, k));  // :335
+            s.sc[j] = sj;
+            kmax = fmaxf(kmax, sj);
         }
         __syncwarp();
         if (lane == 0 && i + SSTAGE < total) issue(i + SSTAGE);  // only this warp read the stage
     }
+    kmax = warp_max(kmax);
+    if (lane == 0) s.wmax[w] = kmax;
     __syncthreads();
 
     // ---------------------------------------------------------------- softmax (:338-344, block_max / block_sum :22-46)
-    // (the butterfly over the four warp values is their max, and (w0 + w2) + (w1 + w3) for the sum)
-    float mx = -INFINITY;
-    for (int j = t; j < L; j += 128) mx = fmaxf(mx, s.sc[j]);
-    mx = warp_max(mx);
-    if (lane == 0) s.wmax[w] = mx;
-    __syncthreads();
+    // (the block max is the max of the warps' maxima of their scores; the sum keeps the reference's order: thread t
+    // over positions t, t + 128, ..., then the warp butterfly and (w0 + w2) + (w1 + w3))
     const float m = fmaxf(fmaxf(s.wmax[0], s.wmax[1]), fmaxf(s.wmax[2], s.wmax[3]));
     float ex[SMAXL / 128];
     float e = 0.f;
