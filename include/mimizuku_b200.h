@@ -203,9 +203,10 @@ int mmz_engine_replay(mmz_engine* e);
  * the step for the whole batch on the engine's stream, as src/model.rs:648-736 does; 2 (the default of the native
  * image) runs the layers of the two halves of a 32-sequence batch on two streams, forked after the embedding and
  * joined before the logits, so that the launch- and latency-bound kernels of one half overlap the other half's. The
- * step's kernels work sequence by sequence and cuBLAS returns the same rows for 16 sequences as for 32, so both
- * settings give identical results; other batch sizes always decode on one lane. Engines on a fatbin image accept
- * only 1. Takes effect at the next step or capture. */
+ * step's kernels work sequence by sequence, so both settings give identical results as long as cuBLAS returns the
+ * same rows for 16 sequences as for 32: the engine checks that once when it is created (the four decoder GEMM shapes,
+ * bit for bit) and otherwise starts on one lane and refuses 2. Other batch sizes always decode on one lane. Engines
+ * on a fatbin image accept only 1. Takes effect at the next step or capture. */
 int mmz_engine_set_lanes(mmz_engine* e, int lanes);
 int mmz_engine_lanes(mmz_engine* e);
 /* Device address of an engine buffer: "tok", "done", "ctr", "align", "logits", "eh", "eqkv", "eatt", "xkv", "mel",

@@ -390,7 +390,6 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
             err_ = "second decoder lane setup failed";
             return;
         }
-        lanes_ = 2;
     }
     const int na = (int)gc_.align_heads.size();
     auto H = [&](size_t n) { return alloc(n * 2); };
@@ -476,7 +475,51 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
             }
         }
     }
-    if (cudaStreamSynchronize(st_) != cudaSuccess) err_ = "engine set-up failed";
+    if (cudaStreamSynchronize(st_) != cudaSuccess) {
+        err_ = "engine set-up failed";
+        return;
+    }
+    if (st2_) {
+        const int r = lanes_rows_match();
+        if (r < 0) {
+            err_ = std::string("decoder lane check failed: ") + last_error();
+            return;
+        }
+        lanes_ok_ = r == 1;
+        lanes_ = lanes_ok_ ? 2 : 1;
+    }
+}
+
+// The two decoder lanes give the one-lane results only if cuBLAS returns, for 16 rows, the rows it returns for 32.
+// Checked once per engine on this GPU and library for the four decoder GEMM shapes, with layer 0's weights, seeded
+// inputs and the same call as the decoding step (each half on its own lane's handle): 1 if every output is equal bit
+// for bit, 0 if not, -1 on an error.
+int Engine::lanes_rows_match() {
+    const int d = dm_.d, ff = dm_.ff, kmax = ff > d ? ff : d, nmax = 3 * d > ff ? 3 * d : ff;
+    const int rows = 2 * LANE_ROWS;
+    void* x = alloc((size_t)rows * kmax * 2);
+    void* y1 = alloc((size_t)rows * nmax * 2);
+    void* y2 = alloc((size_t)rows * nmax * 2);
+    if (!x || !y1 || !y2) return fail("device memory allocation failed");
+    if (launch_fill_normal(x, (long)rows * kmax, 0x5eedull, 0.f, 1.f, st_)) return -1;
+    const DecLayer& l = dec_[0];
+    const struct { const void* w; int n, k; } shapes[4] = {{l.qkv.w, 3 * d, d}, {l.o.w, d, d}, {l.fc1.w, ff, d}, {l.fc2.w, d, ff}};
+    std::vector<uint16_t> a((size_t)rows * nmax), b((size_t)rows * nmax);
+    for (const auto& sh : shapes) {
+        const size_t bytes = (size_t)rows * sh.n * 2;
+        CUDA_CK(cudaMemsetAsync(y1, 0, bytes, st_));
+        CUDA_CK(cudaMemsetAsync(y2, 0, bytes, st_));
+        CK(matmul(true, false, sh.n, rows, sh.k, 1.f, sh.w, sh.k, 0, x, sh.k, 0, 1.f, y1, sh.n, 0, 1, blas_));
+        CK(matmul(true, false, sh.n, LANE_ROWS, sh.k, 1.f, sh.w, sh.k, 0, x, sh.k, 0, 1.f, y2, sh.n, 0, 1, blas_));
+        CUDA_CK(cudaStreamSynchronize(st_));
+        CK(matmul(true, false, sh.n, LANE_ROWS, sh.k, 1.f, sh.w, sh.k, 0, (const char*)x + (size_t)LANE_ROWS * sh.k * 2,
+                  sh.k, 0, 1.f, (char*)y2 + (size_t)LANE_ROWS * sh.n * 2, sh.n, 0, 1, blas2_));
+        CUDA_CK(cudaStreamSynchronize(st2_));
+        CUDA_CK(cudaMemcpy(a.data(), y1, bytes, cudaMemcpyDeviceToHost));
+        CUDA_CK(cudaMemcpy(b.data(), y2, bytes, cudaMemcpyDeviceToHost));
+        if (std::memcmp(a.data(), b.data(), bytes) != 0) return 0;
+    }
+    return 1;
 }
 
 Engine::~Engine() {
@@ -718,6 +761,8 @@ int Engine::reset(const int* prompts, int b, int np) {
 int Engine::set_lanes(int n) {
     if (n != 1 && n != 2) return fail("set_lanes: 1 or 2");
     if (n == 2 && !st2_) return fail("set_lanes: the fatbin image decodes on one lane");
+    if (n == 2 && !lanes_ok_)
+        return fail("set_lanes: cuBLAS on this GPU returns other rows for half batches; decoding stays on one lane");
     lanes_ = n;
     return 0;
 }

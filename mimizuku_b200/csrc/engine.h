@@ -86,9 +86,9 @@ class Engine {
     // decoder-step lanes: 1 runs the step's layers for the whole batch on one stream, as src/model.rs does; 2 (the
     // native image's default) splits a batch of 32 into two halves whose layers run on two streams (one cuBLAS handle
     // and workspace each), forked after the embedding and joined before the logits, so that the latency-bound
-    // launches of one half overlap the other's. Every kernel of the step works row by row and cuBLAS gives the same
-    // rows for 16 sequences as for 32, so both settings give the same results; other batch sizes use one lane. The
-    // fatbin image always uses 1.
+    // launches of one half overlap the other's. Every kernel of the step works row by row, so both settings give the
+    // same results where cuBLAS gives the same rows for 16 sequences as for 32, which the constructor checks
+    // (lanes_rows_match; 1 lane if not); other batch sizes use one lane. The fatbin image always uses 1.
     int set_lanes(int n);
     int lanes() const { return lanes_; }
 
@@ -108,6 +108,7 @@ class Engine {
                          cublasHandle_t h);
     // decoder layer i (model.rs:665-705) for the sequences [r0, r0 + bh) on stream st with cuBLAS handle h
     int dec_layer(int i, int r0, int bh, cudaStream_t st, cublasHandle_t h);
+    int lanes_rows_match();
     void* alloc(size_t bytes);
     int decode_and_times(const int* frames, int n, const int* prompt, int np, int max_steps, bool graph, int threads,
                          int* tokens, int* lens, float* times, double* stage_s,
@@ -123,6 +124,7 @@ class Engine {
     cudaStream_t st_ = nullptr;
     cublasHandle_t blas_ = nullptr;
     int lanes_ = 1;
+    bool lanes_ok_ = false;          // lanes_rows_match() found the half-batch rows equal
     cudaStream_t st2_ = nullptr;     // second decoder lane
     cublasHandle_t blas2_ = nullptr;
     void* ws2_ = nullptr;
