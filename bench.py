@@ -1,8 +1,9 @@
 """Benchmark: end-to-end Whisper large-v3 transcription throughput (clips/s) on B200, 32 synthetic 30 s clips per GPU,
-random-init weights, 224 fixed greedy tokens, token timestamps by DTW (the metric's other two
-figures, encoder-attention TFLOP/s and decoder-attention HBM GB/s, are reported beside it).
+random-init weights, 224 fixed greedy tokens, token timestamps by DTW; the metric's other two figures, encoder-attention
+TFLOP/s and decoder-attention HBM GB/s, are reported beside it. --model large-v3-turbo runs the 4-decoder-layer model
+(the multi-GPU configuration: 32 clips per GPU at 1, 2, 4 and 8 GPUs).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference] [--model M] [--clips-per-gpu C]
     torchrun --nproc-per-node N bench.py --gpus N ...        (one process per GPU, 32 clips per GPU: weak scaling)
 
 A step is one batch of 32 clips per GPU. `value` times the GPU pipeline (encoder for 4 groups of 8 clips, then 227
@@ -25,9 +26,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CLIPS_PER_GPU = 32
+CLIPS_PER_GPU = 32  # default; --clips-per-gpu
 NEW_TOKENS = 224
-METRIC = "clips/s (30 s, large-v3, batch 32)"
 REF_FATBIN = os.path.join(ROOT, "oracle", "_ref", "whisper_ref.fatbin")
 
 
@@ -122,36 +122,38 @@ def features_gpu(ys, n_mels, torch):
     return best, audio.numel() * 4
 
 
-def cpu_baseline(threads):
-    """The oracle's multithreaded f32 CPU attention (the reference has no CPU attention path) on a bounded sample:
-    one clip's encoder attention for one layer (20 heads x 1500 x 1500 x 64) and one decoder step's cross-attention
-    for one sequence and layer, scaled to a whole clip of large-v3 (32 encoder layers; 227 steps x 32 decoder
-    layers)."""
+def cpu_baseline(cfg, threads):
+    """The oracle's multithreaded f32 CPU restatement of the path's attention (the reference has no CPU attention
+    path; oracle/oracle_fast.c, AVX2/F16C/FMA), timed on whole clips of the benchmark's workload: one clip's encoder
+    attention (every encoder layer, all heads, 1500 x 1500 x 64, on `threads` threads), then `threads` clips' decoder
+    attention, one clip per thread (227 decoding steps x every decoder layer: kv_write, causal self-attention and the
+    cross-attention over 1500 positions, with the reference kernels' fp16 rounding points). clips/s = 1 / (encoder
+    seconds of one clip + decoder seconds / clips)."""
+    import ctypes
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import _oracle as O
     rng = np.random.default_rng(0)
-    d, nh = 1280, 20
+    d, nh = cfg.d, cfg.heads
     qkv = O.normal16(rng, (1, 1500, 3 * d))
     out = np.zeros((1, 1500, d), np.float16)
     t0 = time.perf_counter()
-    O.orc.orc_cpu_enc_attn(O.u16(qkv), O.u16(out), 1, d, nh, 1500, threads)
+    for _ in range(cfg.enc_layers):
+        O.orc.orc_cpu_enc_attn(O.u16(qkv), O.u16(out), 1, d, nh, 1500, threads)
     t_enc = time.perf_counter() - t0
-    q = O.normal16(rng, (d,))
-    kv = O.normal16(rng, (2, nh, 1500, 64))
-    o = np.zeros(d, np.float16)
-    t0 = time.perf_counter()
-    reps = 8
-    for _ in range(reps):
-        O.orc.orc_cpu_cross_step(O.u16(q), O.u16(kv), O.u16(o), nh)
-    t_cross = (time.perf_counter() - t0) / reps
-    per_clip = 32 * t_enc + (NEW_TOKENS + 3) * 32 * t_cross
-    return {"value": round(1.0 / per_clip, 6), "unit": "clips/s", "cores": threads, "kind": "port",
-            "sample": (f"attention only: 1 clip x 1 encoder layer ({t_enc:.2f} s on {threads} threads) + 1 decoder "
-                       f"step's cross-attention of 1 sequence x 1 layer ({t_cross * 1e3:.2f} ms, 1 thread), scaled to "
-                       "32 encoder layers + 227 steps x 32 decoder layers per clip")}
+    sec = ctypes.c_double()
+    np_ = len(cfg.prompt)
+    steps = np_ - 1 + NEW_TOKENS
+    O.orc.orc_cpu_dec_attn_clips(threads, cfg.dec_layers, nh, np_, steps, cfg.max_t, ctypes.byref(sec))
+    t_dec = sec.value
+    per_clip = t_enc + t_dec / threads
+    return {"value": round(1.0 / per_clip, 5), "unit": "clips/s", "cores": threads, "kind": "port",
+            "sample": (f"attention of whole clips: 1 clip's encoder ({cfg.enc_layers} layers x {nh} heads, "
+                       f"{t_enc:.2f} s on {threads} threads) + {threads} clips' decoder ({steps} steps x "
+                       f"{cfg.dec_layers} layers of self- and cross-attention, one clip per thread, {t_dec:.2f} s)"),
+            "enc_s_per_clip": round(t_enc, 3), "dec_s_per_clip": round(t_dec / threads, 3)}
 
 
-def kernel_rooflines(e, cfg, torch, impl):
+def kernel_rooflines(e, cfg, torch, impl, B):
     """Live CUDA-event timings of the hot kernels, replayed from a CUDA graph on the engine's stream and buffers
     (inputs larger than L2):
     cross-attention (the dominant kernel of the decoding step), self-attention at the mean context, and encoder
@@ -159,7 +161,7 @@ def kernel_rooflines(e, cfg, torch, impl):
     self_attn, enc_flash) with src/model.rs's launch geometry on the same buffers."""
     import mimizuku_b200 as m
     st = torch.cuda.ExternalStream(e.stream)
-    B, d, nl, mt, na, nh = CLIPS_PER_GPU, cfg.d, cfg.dec_layers, cfg.max_t, e.na, cfg.heads
+    d, nl, mt, na, nh = cfg.d, cfg.dec_layers, cfg.max_t, e.na, cfg.heads
     buf = e.buffer
     ctr = torch.tensor([100, 0, 0, 0], dtype=torch.int32, device="cuda")
     done = torch.zeros(B, dtype=torch.int32, device="cuda")
@@ -249,7 +251,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--threads", type=int, default=0, help="host threads for DTW (0 = all)")
+    ap.add_argument("--model", choices=["large-v3", "large-v3-turbo"], default="large-v3")
+    ap.add_argument("--clips-per-gpu", type=int, default=CLIPS_PER_GPU, help="clips per GPU (a multiple of 8, <= 32)")
     args = ap.parse_args()
+    nb = args.clips_per_gpu
+    if nb < 8 or nb > 32 or nb % 8:
+        ap.error("--clips-per-gpu: a multiple of 8 from 8 to 32 (encoder groups of 8 clips)")
     if args.warmup < 3:
         args.warmup = 3
 
@@ -272,16 +279,17 @@ def main():
 
     import mimizuku_b200 as m
     m.init(local)
-    cfg = m.LARGE_V3
+    cfg = m.LARGE_V3 if args.model == "large-v3" else m.LARGE_V3_TURBO
+    metric = f"clips/s (30 s, {cfg.name}, batch {nb})"
     hbm_peak, tc_peak, peak_src = peaks()
     n_threads = args.threads or max(1, (os.cpu_count() or 8) // max(1, world))
 
-    mel, frames, clips, t_feat_host = make_features(cfg.n_mels, rank * CLIPS_PER_GPU, CLIPS_PER_GPU, n_threads)
+    mel, frames, clips, t_feat_host = make_features(cfg.n_mels, rank * nb, nb, n_threads)
     # the end-to-end inputs live in pinned host memory (page-locked: the copies to the device run at full speed)
     mel = torch.from_numpy(mel).pin_memory().numpy()
     clips = [torch.from_numpy(y).pin_memory().numpy() for y in clips]
     kimg = REF_FATBIN if args.impl == "reference" else None
-    e = m.Engine(cfg, bmax=CLIPS_PER_GPU, eg=8, device=local, kernel_image=kimg, seed=1234,
+    e = m.Engine(cfg, bmax=nb, eg=8, device=local, kernel_image=kimg, seed=1234,
                  suppress=[cfg.eos])
     mel16 = torch.from_numpy(mel.astype(np.float16)).cuda()
     prompt = np.array(cfg.prompt, np.int32)
@@ -290,22 +298,22 @@ def main():
     st = torch.cuda.ExternalStream(e.stream)
 
     if args.impl == "native":  # the timestamp cost and DTW run on the GPU (the reference does them on the host)
-        rc_dev = torch.tensor([NEW_TOKENS - 1] * CLIPS_PER_GPU + [int(f) // 2 for f in frames], dtype=torch.int32,
+        rc_dev = torch.tensor([NEW_TOKENS - 1] * nb + [int(f) // 2 for f in frames], dtype=torch.int32,
                               device="cuda")
-        cost_dev = torch.empty((CLIPS_PER_GPU, cfg.max_t, 1500), dtype=torch.float32, device="cuda")
-        times_dev = torch.empty((CLIPS_PER_GPU, cfg.max_t), dtype=torch.float32, device="cuda")
+        cost_dev = torch.empty((nb, cfg.max_t, 1500), dtype=torch.float32, device="cuda")
+        times_dev = torch.empty((nb, cfg.max_t), dtype=torch.float32, device="cuda")
 
     def gpu_pipeline():
-        for g0 in range(0, CLIPS_PER_GPU, 8):
+        for g0 in range(0, nb, 8):
             e.encode(mel16[g0].data_ptr(), 8, g0)
-        e.reset(np.tile(prompt, (CLIPS_PER_GPU, 1)))
+        e.reset(np.tile(prompt, (nb, 1)))
         for _ in range(steps_dec):
             e.replay()
         if args.impl == "native":
-            m.align_cost(e.buffer("align"), rc_dev[:CLIPS_PER_GPU], rc_dev[CLIPS_PER_GPU:], np_, cfg.max_t, e.na,
-                         cost_dev, n=CLIPS_PER_GPU, stream=e.stream)
-            m.dtw_times(cost_dev, rc_dev[:CLIPS_PER_GPU], rc_dev[CLIPS_PER_GPU:], cfg.max_t, times_dev,
-                        n=CLIPS_PER_GPU, stream=e.stream)
+            m.align_cost(e.buffer("align"), rc_dev[:nb], rc_dev[nb:], np_, cfg.max_t, e.na,
+                         cost_dev, n=nb, stream=e.stream)
+            m.dtw_times(cost_dev, rc_dev[:nb], rc_dev[nb:], cfg.max_t, times_dev,
+                        n=nb, stream=e.stream)
 
     def barrier():
         if dist:
@@ -319,8 +327,8 @@ def main():
         return t.item()
 
     # capture the decoding step once (outside every timed region), as transcribe.rs:122-131 does
-    e.reset(np.tile(prompt, (CLIPS_PER_GPU, 1)))
-    e.capture(CLIPS_PER_GPU, np_)
+    e.reset(np.tile(prompt, (nb, 1)))
+    e.capture(nb, np_)
     for _ in range(args.warmup):
         gpu_pipeline()
     e.sync()
@@ -366,25 +374,30 @@ def main():
         torch.cuda.synchronize()
         t_audio = max_over_ranks(time.perf_counter() - t0)
 
-    kr = kernel_rooflines(e, cfg, torch, args.impl)
+    kr = kernel_rooflines(e, cfg, torch, args.impl, nb)
     bx, tx = kr["cross"]
     bs_, ts_ = kr["self"]
     fe, te = kr["enc"]
-    n_total = CLIPS_PER_GPU * world
+    n_total = nb * world
     value = n_total * args.steps / t_dev
     e2e = n_total * args.steps / t_e2e
-    h2d = mel.nbytes + 4 * CLIPS_PER_GPU * np_
+    # the log-mel crosses as fp32 for the native image (rounded on the device) and as fp16 for the reference's (rounded
+    # on the host, src/model.rs:549); plus the prompt tokens
+    h2d = (mel.nbytes if args.impl == "native" else mel.nbytes // 2) + 4 * nb * np_
     d2h = e.d2h_bytes  # tokens, and the recorded probabilities (reference) or the DTW cost rows (native)
+    # DRAM bytes per launch of the native cross-attention kernels from an ncu capture of the large-v3 batch-32 layer
+    # (profiles/cross_attn_traffic.txt); the reference's kernels and other shapes were not captured: null
     traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "cross_attn_traffic.txt")) as f:
-            for ln in f:
-                if ln.startswith("cross_attn_bytes_per_launch"):
-                    traffic = int(ln.split()[1])
-    except OSError:
-        pass
+    if args.impl == "native" and cfg.d == 1280 and nb == 32:
+        try:
+            with open(os.path.join(ROOT, "profiles", "cross_attn_traffic.txt")) as f:
+                for ln in f:
+                    if ln.startswith("cross_attn_bytes_per_launch"):
+                        traffic = int(ln.split()[1])
+        except OSError:
+            pass
     line = {
-        "metric": METRIC,
+        "metric": metric,
         "value": round(value, 3),
         "unit": "clips/s",
         "n_gpus": world,
@@ -396,10 +409,13 @@ def main():
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded 30 s clips: 1-8 sinusoids 80-4000 Hz + noise at 10 dB SNR; random-init weights)",
-        "config": {"workload": "e2e whisper large-v3 (random init), 32 clips of 30 s per GPU, encoder groups of 8, "
-                               "224 fixed greedy tokens (eos suppressed), 10 alignment heads, DTW timestamps",
-                   "clips_per_gpu": CLIPS_PER_GPU, "new_tokens": NEW_TOKENS, "decoder_lanes": e.lanes,
-                   "l2": "inputs larger than L2: cross k/v 7.9 GB and weights 3.1 GB per GPU are streamed each step"},
+        "config": {"workload": (f"e2e whisper {cfg.name} (random init, {cfg.enc_layers} encoder + {cfg.dec_layers} "
+                                f"decoder layers), {nb} clips of 30 s per GPU, encoder groups of 8, {NEW_TOKENS} fixed "
+                                f"greedy tokens (eos suppressed), {e.na} alignment heads, DTW timestamps"),
+                   "model": cfg.name,
+                   "clips_per_gpu": nb, "new_tokens": NEW_TOKENS, "decoder_lanes": e.lanes,
+                   "l2": (f"inputs larger than L2: cross k/v {nb * cfg.dec_layers * 2 * cfg.d * 1500 * 2 / 1e9:.2f} GB "
+                          "and the decoder weights per GPU are streamed each step")},
         "e2e": {"value": round(e2e, 3), "unit": "clips/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
                 "stage_s_per_step": [round(x / args.steps, 4) for x in stages]},
@@ -423,7 +439,7 @@ def main():
                                   "what": "the C-ABI transcribe from host audio: log-mel on the GPU, then as e2e"}
     if args.impl == "native":  # log-mel is outside the clips/s metric (features are reported separately)
         t_feat_gpu, feat_h2d = features_gpu(clips, cfg.n_mels, torch)
-        line["features"] = {"clips": CLIPS_PER_GPU, "host_s": round(t_feat_host, 4), "host_threads": n_threads,
+        line["features"] = {"clips": nb, "host_s": round(t_feat_host, 4), "host_threads": n_threads,
                             "gpu_s": round(t_feat_gpu, 5), "gpu_h2d_bytes": int(feat_h2d),
                             "what": "log-mel of 30 s clips (src/audio.rs): host restatement vs the GPU kernels "
                                     "(host-to-device copy of the samples included)"}
@@ -432,7 +448,7 @@ def main():
         line["reference_kind"] = ("the reference's own kernels (kernels/whisper.cu, compute_80 PTX JIT-compiled on "
                                   "the B200) driven by this repository's C++ restatement of its host")
     if rank == 0 and world == 1 and args.impl == "native":
-        line["cpu_baseline"] = cpu_baseline(os.cpu_count() or 1)
+        line["cpu_baseline"] = cpu_baseline(cfg, min(32, os.cpu_count() or 1))
     if rank == 0:
         print(json.dumps(line), flush=True)
     e.close()

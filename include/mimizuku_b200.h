@@ -22,8 +22,9 @@ extern "C" {
 
 /* ---------------------------------------------------------------- library */
 
-/* Initialises the library on `device` and makes it current (status word, kernel attributes). Replaces the set-up
- * part of Gpu::new (src/gpu.rs:122-137). */
+/* Initialises the library on `device` and makes it current (status word, kernel attributes, the static scratch of
+ * mmz_cross_attn_noalloc). Calling it again re-resolves those device addresses, as is needed after a
+ * cudaDeviceReset. Replaces the set-up part of Gpu::new (src/gpu.rs:122-137). */
 int mmz_init(int device);
 const char* mmz_last_error(void);
 /* Reads and clears the device status word of the current device: code[0] error (0 none, 1 wait timed out,
@@ -84,9 +85,11 @@ unsigned long long mmz_cross_attn_scratch_bytes(int batch, int d);
  * forbids cudaMalloc after start-up, or a loop that cannot take cudaMalloc's implicit synchronisation): the same
  * kernels and results, with the scratch in a static device array of the library (7.9 MB per device that loads the
  * library, held until the process exits) instead of a caller buffer. It allocates nothing. Limit: batch x heads <= 640
- * (32 sequences of a 20-head model); larger calls return an error. The first call on a device resolves the array's
- * address and should come before any stream capture. Every call shares the array; calls that overlap on the GPU
- * race on it and must be serialised by the caller. No counterpart in the reference. */
+ * (32 sequences of a 20-head model); larger calls return an error. mmz_init resolves the array's device address
+ * and caches it (a call on a device without a prior mmz_init resolves it itself, which should then come before any
+ * stream capture); after a cudaDeviceReset the cached address is invalid until mmz_init is called again on that
+ * device. Every call shares the array, which keeps the last call's contents; calls that overlap on the GPU race on
+ * it and must be serialised by the caller. No counterpart in the reference. */
 int mmz_cross_attn_noalloc(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
                            const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* stream);
 
@@ -206,7 +209,8 @@ int mmz_engine_replay(mmz_engine* e);
  * step's kernels work sequence by sequence, so both settings give identical results as long as cuBLAS returns the
  * same rows for 16 sequences as for 32: the engine checks that once when it is created (the four decoder GEMM shapes,
  * bit for bit) and otherwise starts on one lane and refuses 2. Other batch sizes always decode on one lane. Engines
- * on a fatbin image accept only 1. Takes effect at the next step or capture. */
+ * on a fatbin image, and engines created for fewer than 32 sequences (bmax < 32), have no second lane and accept
+ * only 1. Takes effect at the next step or capture. */
 int mmz_engine_set_lanes(mmz_engine* e, int lanes);
 int mmz_engine_lanes(mmz_engine* e);
 /* Device address of an engine buffer: "tok", "done", "ctr", "align", "logits", "eh", "eqkv", "eatt", "xkv", "mel",

@@ -22,8 +22,9 @@ extern "C" {
 
 int mmz_init(int device) {
     if (cudaSetDevice(device) != cudaSuccess) return failf("cudaSetDevice(%d) failed", device);
-    DevCtx& c = dev_ctx();
-    return c.ok ? 0 : fail(c.err);
+    DevCtx& c = dev_ctx_refresh();
+    if (!c.ok) return fail(c.err);
+    return noalloc_resolve();
 }
 
 const char* mmz_last_error(void) { return last_error(); }

@@ -10,9 +10,10 @@
 //
 // The array is shared by every call on a device and keeps the last call's contents; nothing in it needs to start at
 // zero (every value a call reads was written earlier in the same call). Calls that overlap on the GPU (other streams,
-// other threads) race on the array and must be serialised by the caller. The first call on a device resolves the
-// array's device address (cudaGetSymbolAddress, with that device current): make that first call before any stream
-// capture.
+// other threads) race on the array and must be serialised by the caller. mmz_init resolves the array's device address
+// (cudaGetSymbolAddress, with that device current) and caches it per device, so the entry point itself only reads the
+// cached pointer; a device reset (cudaDeviceReset) invalidates it, and mmz_init must be called again on that device
+// before the next call. Without a prior mmz_init the first call resolves the address itself.
 #include <mutex>
 
 #include "../../include/mimizuku_b200.h"
@@ -30,19 +31,38 @@ static __device__ __align__(256) unsigned char g_cross_scratch[NOALLOC_BYTES];
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_addr[64];  // device address of g_cross_scratch, per device
 
-// The array's device address on the current device, resolved once per device. In host code the symbol
-// g_cross_scratch is only a host-side stand-in; the kernels must be given this address.
-static int noalloc_scratch(void** out) {
+static int current_dev() {
     int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail("cross_attn_noalloc: no CUDA device");
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    return dev;
+}
+
+// Resolves the array's device address on the current device and caches it (called by mmz_init, with the device
+// current; again after a device reset). In host code the symbol g_cross_scratch is only a host-side stand-in; the
+// kernels must be given this address.
+int noalloc_resolve() {
+    const int dev = current_dev();
+    if (dev < 0) return fail("cross_attn_noalloc: no CUDA device");
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_cross_scratch);
+    if (e != cudaSuccess || !p)
+        return failf("cross_attn_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_cross_scratch);
-        if (e != cudaSuccess || !p)
-            return failf("cross_attn_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-        g_noalloc_addr[dev] = p;
+    g_noalloc_addr[dev] = p;
+    return 0;
+}
+
+// the cached address of the current device (resolved here if mmz_init was not called on it)
+static int noalloc_scratch(void** out) {
+    const int dev = current_dev();
+    if (dev < 0) return fail("cross_attn_noalloc: no CUDA device");
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        *out = g_noalloc_addr[dev];
     }
+    if (*out) return 0;
+    if (noalloc_resolve()) return -1;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
     *out = g_noalloc_addr[dev];
     return 0;
 }

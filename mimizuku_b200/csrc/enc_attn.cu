@@ -67,7 +67,7 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// grid (12 query tiles, heads, clips), block 384, dynamic shared memory sizeof(Smem)
+// grid (12 query tiles, heads, clips), block NTHREADS (320), dynamic shared memory sizeof(Smem)
 __global__ void __launch_bounds__(NTHREADS, 2)
     enc_flash_kernel(const __grid_constant__ CUtensorMap qkv_map, h16* __restrict__ out, int d, unsigned* status,
                      unsigned long long limit_ns) {

@@ -380,7 +380,7 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         err_ = "cuBLAS workspace";
         return;
     }
-    if (k_->native()) {  // the second decoder lane: its own stream, cuBLAS handle and workspace
+    if (k_->native() && bmax_ >= 2 * LANE_ROWS) {  // the second decoder lane: its own stream, cuBLAS handle, workspace
         ws2_ = alloc(WS_BYTES);
         if (!ws2_ || cudaStreamCreateWithFlags(&st2_, cudaStreamNonBlocking) != cudaSuccess ||
             cublasCreate(&blas2_) != CUBLAS_STATUS_SUCCESS || cublasSetStream(blas2_, st2_) != CUBLAS_STATUS_SUCCESS ||
@@ -495,12 +495,22 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
 // inputs and the same call as the decoding step (each half on its own lane's handle): 1 if every output is equal bit
 // for bit, 0 if not, -1 on an error.
 int Engine::lanes_rows_match() {
+    // a test hook: MMZ_TEST_LANES_DIFFER=1 makes the check report different rows, so that the one-lane fallback can be
+    // exercised on hardware where cuBLAS does return equal rows
+    if (const char* t = getenv("MMZ_TEST_LANES_DIFFER"))
+        if (t[0] == '1') return 0;
+    // the probe buffers live only for the check (plain allocations, freed on every return path)
+    struct Probe {
+        void* p[3] = {nullptr, nullptr, nullptr};
+        ~Probe() { for (void* q : p) if (q) cudaFree(q); }
+    } pb;
     const int d = dm_.d, ff = dm_.ff, kmax = ff > d ? ff : d, nmax = 3 * d > ff ? 3 * d : ff;
     const int rows = 2 * LANE_ROWS;
-    void* x = alloc((size_t)rows * kmax * 2);
-    void* y1 = alloc((size_t)rows * nmax * 2);
-    void* y2 = alloc((size_t)rows * nmax * 2);
-    if (!x || !y1 || !y2) return fail("device memory allocation failed");
+    if (cudaMalloc(&pb.p[0], (size_t)rows * kmax * 2) != cudaSuccess ||
+        cudaMalloc(&pb.p[1], (size_t)rows * nmax * 2) != cudaSuccess ||
+        cudaMalloc(&pb.p[2], (size_t)rows * nmax * 2) != cudaSuccess)
+        return fail("device memory allocation failed");
+    void *x = pb.p[0], *y1 = pb.p[1], *y2 = pb.p[2];
     if (launch_fill_normal(x, (long)rows * kmax, 0x5eedull, 0.f, 1.f, st_)) return -1;
     const DecLayer& l = dec_[0];
     const struct { const void* w; int n, k; } shapes[4] = {{l.qkv.w, 3 * d, d}, {l.o.w, d, d}, {l.fc1.w, ff, d}, {l.fc2.w, d, ff}};
@@ -760,7 +770,8 @@ int Engine::reset(const int* prompts, int b, int np) {
 
 int Engine::set_lanes(int n) {
     if (n != 1 && n != 2) return fail("set_lanes: 1 or 2");
-    if (n == 2 && !st2_) return fail("set_lanes: the fatbin image decodes on one lane");
+    if (n == 2 && !st2_)
+        return fail("set_lanes: two lanes need the native kernel image and an engine for at least 32 sequences");
     if (n == 2 && !lanes_ok_)
         return fail("set_lanes: cuBLAS on this GPU returns other rows for half batches; decoding stays on one lane");
     lanes_ = n;
@@ -880,13 +891,28 @@ int Engine::transcribe(const float* mel, const int* frames, int n, const int* pr
                        bool graph, int threads, int* tokens, int* lens, float* times, double* stage_s) {
     if (n < 1 || n > bmax_) return fail("transcribe: 1..bmax clips per call");
     const auto t0 = std::chrono::steady_clock::now();
-    // fp32 log-mel to the device, rounded to fp16 there (the reference rounds on the host with f2h, model.rs:549)
     const size_t per = (size_t)dm_.n_mels * NFRAMES;
-    for (int g0 = 0; g0 < n; g0 += eg_) {
-        const int gn = std::min(eg_, n - g0);
-        CUDA_CK(cudaMemcpyAsync(mel32_, mel + per * g0, per * gn * 4, cudaMemcpyHostToDevice, st_));
-        CK(launch_f32_to_f16(mel32_, mel_, (long)(per * gn), st_));
-        CK(encode_dev(mel_, gn, g0));
+    if (k_->native()) {
+        // fp32 log-mel to the device, rounded to fp16 there by this library's kernel
+        for (int g0 = 0; g0 < n; g0 += eg_) {
+            const int gn = std::min(eg_, n - g0);
+            CUDA_CK(cudaMemcpyAsync(mel32_, mel + per * g0, per * gn * 4, cudaMemcpyHostToDevice, st_));
+            CK(launch_f32_to_f16(mel32_, mel_, (long)(per * gn), st_));
+            k_->launches++;
+            CK(encode_dev(mel_, gn, g0));
+        }
+    } else {
+        // the reference's way (model.rs:549-550, gpu.rs:160-163): each group rounded to fp16 on the host with f2h,
+        // uploaded, and the stream synchronised before the host buffer is reused
+        std::vector<uint16_t> host(per * (size_t)eg_);
+        for (int g0 = 0; g0 < n; g0 += eg_) {
+            const int gn = std::min(eg_, n - g0);
+            const float* src = mel + per * g0;
+            for (size_t i = 0; i < per * gn; i++) host[i] = f2h(src[i]);
+            CUDA_CK(cudaMemcpyAsync(mel_, host.data(), per * gn * 2, cudaMemcpyHostToDevice, st_));
+            CUDA_CK(cudaStreamSynchronize(st_));
+            CK(encode_dev(mel_, gn, g0));
+        }
     }
     CUDA_CK(cudaStreamSynchronize(st_));
     return decode_and_times(frames, n, prompt, np, max_steps, graph, threads, tokens, lens, times, stage_s, t0);

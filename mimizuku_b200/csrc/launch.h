@@ -18,6 +18,10 @@ struct DevCtx {
 
 // context of the current device, initialised on first use (call mmz_init before any stream capture)
 DevCtx& dev_ctx();
+// the same, initialised again (device addresses re-resolved: after a cudaDeviceReset they change); mmz_init calls it
+DevCtx& dev_ctx_refresh();
+// resolves the device address of mmz_cross_attn_noalloc's static scratch array on the current device (cross_noalloc.cu)
+int noalloc_resolve();
 // records msg as the calling thread's last error and returns -1
 int fail(const char* msg);
 int failf(const char* fmt, ...);

@@ -44,34 +44,27 @@ int check_pdl(cudaError_t e, const char* what) {
 static std::mutex g_mu;
 static DevCtx g_ctx[64];
 
-DevCtx& dev_ctx() {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-        static DevCtx bad;
-        bad.ok = false;
-        bad.err = "no CUDA device";
-        return bad;
-    }
-    DevCtx& c = g_ctx[dev];
-    if (c.inited) return c;
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (c.inited) return c;
+// Fills c for device dev (current): device checks, the status word's device address, kernel attributes. Called with
+// g_mu held; c.ok is set only at the end, so a context that was ok stays usable while it is refreshed.
+static void init_ctx(DevCtx& c, int dev) {
     c.inited = true;
-    c.ok = false;
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+        c.ok = false;
         c.err = "cudaGetDeviceProperties failed";
-        return c;
+        return;
     }
     if (prop.major != 10 || prop.minor != 0) {
+        c.ok = false;
         c.err = "the mimizuku_b200 kernels are built for sm_100a (B200) only";
-        return c;
+        return;
     }
     c.sms = prop.multiProcessorCount;
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) {
+        c.ok = false;
         c.err = "cudaGetSymbolAddress(status) failed";
-        return c;
+        return;
     }
     c.status = (unsigned*)p;
     if (const char* s = getenv("MMZ_WAIT_LIMIT_MS")) c.limit_ns = (unsigned long long)atoll(s) * 1000000ull;
@@ -82,7 +75,35 @@ DevCtx& dev_ctx() {
     cudaGetLastError();
     c.ok = true;
     c.err = "";
+}
+
+static int current_device() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+    return dev;
+}
+
+DevCtx& dev_ctx() {
+    const int dev = current_device();
+    if (dev < 0) {
+        static DevCtx bad;
+        bad.ok = false;
+        bad.err = "no CUDA device";
+        return bad;
+    }
+    DevCtx& c = g_ctx[dev];
+    if (c.inited) return c;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!c.inited) init_ctx(c, dev);
     return c;
+}
+
+DevCtx& dev_ctx_refresh() {
+    const int dev = current_device();
+    if (dev < 0) return dev_ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    init_ctx(g_ctx[dev], dev);
+    return g_ctx[dev];
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point

@@ -42,6 +42,12 @@ void orc_enc_attn_f64(const uint16_t* qkv, double* out, int g, int d, int r0, in
 void orc_cpu_enc_attn(const uint16_t* qkv, uint16_t* out, int g, int d, int heads, int rows, int nthreads);
 /* oracle_fast.c: one sequence's cross-attention step (kernels/whisper.cu:368-449), kv [2][nh][1500][64] */
 double orc_cpu_cross_step(const uint16_t* q, const uint16_t* kv, uint16_t* out, int nh);
+/* oracle_fast.c: the decoder attention of nseq whole clips on nseq threads (steps decoding steps after an np-token
+ * prompt; per step and layer kv_write + causal self-attention and the cross-attention over 1500 positions,
+ * src/model.rs:660-705, with kernels/whisper.cu's rounding points), AVX2/F16C/FMA, synthetic fp16 inputs filled
+ * before the timed part (one cross k/v shared read-only, each thread starting at another layer; caches per thread);
+ * *seconds = wall time of the attention work; returns a checksum of the outputs. */
+double orc_cpu_dec_attn_clips(int nseq, int nl, int nh, int np, int steps, int max_t, double* seconds);
 
 /* kernels/whisper.cu:310-353 (kv_write then self_attn) at position p = ctr[0]: the caches hold rows 0..p-1, row p
  * is taken from qkv and also written to the caches. Rounds q*0.125, scores and probabilities to fp16. */

@@ -34,6 +34,7 @@ def _load():
         "orc_enc_attn_f64": (None, [_U16P, _DP, _I, _I, _I, _I, _I]),
         "orc_cpu_enc_attn": (None, [_U16P, _U16P, _I, _I, _I, _I, _I]),
         "orc_cpu_cross_step": (ctypes.c_double, [_U16P, _U16P, _U16P, _I]),
+        "orc_cpu_dec_attn_clips": (ctypes.c_double, [_I, _I, _I, _I, _I, _I, _DP]),
         "orc_self_attn": (None, [_U16P, _U16P, _U16P, _U16P, _I, _IP, _I, _I, _I]),
         "orc_self_attn_f64": (None, [_U16P, _U16P, _U16P, _DP, _I, _IP, _I, _I, _I]),
         "orc_cross_attn": (None, [_U16P, _U16P, _U16P, _U16P, _IP, _I, _IP, _I, _I, _I, _I, _I, _I]),
@@ -184,6 +185,11 @@ def d2h(dst, src_ptr):
 
 def h2d(dst_ptr, src):
     assert _cudart().cudaMemcpy(dst_ptr, np.ascontiguousarray(src).ctypes.data, src.nbytes, 1) == 0
+
+
+def d2d(dst_ptr, src_ptr, nbytes):
+    """Copies nbytes between two device addresses (synchronous with respect to the host)."""
+    assert _cudart().cudaMemcpy(dst_ptr, src_ptr, nbytes, 3) == 0
 
 
 # ------------------------------------------------------------------ seeded inputs

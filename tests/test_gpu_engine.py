@@ -205,12 +205,11 @@ def test_transcribe_from_audio_is_transcribe_of_the_gpu_features(cuda):
     e.close()
 
 
-@pytest.mark.parametrize("name,b,new", [("TINY", 32, 24), ("TINY", 9, 24), ("LARGE_V3_TURBO", 32, 12)])
+@pytest.mark.parametrize("name,b,new", [("TINY", 32, 24), ("LARGE_V3_TURBO", 32, 12)])
 def test_two_decoder_lanes_match_one(cuda, name, b, new):
     """Two decoder lanes (the halves of a 32-sequence batch on two streams, the native image's default) give exactly
     the tokens, alignment rows and token times of one lane (the whole batch on one stream, as src/model.rs runs the
-    step), in the captured graph and eagerly; the turbo case has large-v3's decoder GEMM shapes. A batch of 9 decodes
-    on one lane whatever the setting."""
+    step), in the captured graph and eagerly; the turbo case has large-v3's decoder GEMM shapes."""
     import mimizuku_b200 as m
     cfg = getattr(m, name)
     mel, frames = _clips(b, cfg.n_mels, seed=2)
@@ -238,3 +237,37 @@ def test_fatbin_engine_decodes_on_one_lane(cuda, ref):
     with pytest.raises(m.MmzError):
         e.lanes = 2
     e.close()
+
+
+def test_engine_for_fewer_than_32_sequences_has_one_lane(cuda):
+    """An engine created for fewer than 32 sequences sets up no second lane: it reports one lane and refuses two."""
+    import mimizuku_b200 as m
+    e = m.Engine(m.TINY, bmax=9, eg=8, seed=5, suppress=[m.TINY.eos])
+    assert e.lanes == 1
+    with pytest.raises(m.MmzError):
+        e.lanes = 2
+    e.close()
+
+
+def test_lane_check_failure_falls_back_to_one_lane(cuda, monkeypatch):
+    """When the creation-time check finds cuBLAS's half-batch rows different from the whole batch's (forced here by
+    the library's test hook), the engine starts on one lane, refuses two, and decodes exactly as an engine that
+    passed the check and was set to one lane."""
+    import mimizuku_b200 as m
+    cfg, b, new = m.TINY, 32, 12
+    mel, frames = _clips(b, cfg.n_mels, seed=7)
+    monkeypatch.setenv("MMZ_TEST_LANES_DIFFER", "1")
+    e = m.Engine(cfg, bmax=b, eg=8, seed=5, suppress=[cfg.eos])
+    monkeypatch.delenv("MMZ_TEST_LANES_DIFFER")
+    assert e.lanes == 1
+    with pytest.raises(m.MmzError):
+        e.lanes = 2
+    r = e.transcribe(mel, frames, max_new=new)
+    e.close()
+    ok = m.Engine(cfg, bmax=b, eg=8, seed=5, suppress=[cfg.eos])
+    assert ok.lanes == 2
+    ok.lanes = 1
+    x = ok.transcribe(mel, frames, max_new=new)
+    ok.close()
+    for k in ("tokens", "lens", "times"):
+        assert np.array_equal(r[k], x[k]), k
