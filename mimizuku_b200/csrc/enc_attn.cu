@@ -141,16 +141,21 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     } else if (warp == 1) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t qa = smem_u32(s.q);
+            // Shared-memory descriptors are formed once; a K step, a ring stage or a V row block only advances the
+            // start-address field (16-byte units; every address of the CTA's shared memory fits its 14 bits). This
+            // keeps each MMA's issue to a few instructions: recomputing the descriptor per MMA cost the issuing
+            // thread ~50 cycles of dependent integer work per MMA.
+            const uint64_t qd = sdesc_sw128(smem_u32(s.q), 16, SBO);
+            const uint64_t kd0 = sdesc_sw128(smem_u32(s.k[0]), 16, SBO);
+            const uint64_t vd0 = sdesc_sw128(smem_u32(s.v[0]), TILE, SBO);
+            constexpr uint64_t STAGE = TILE >> 4, KSTEP = 32 >> 4, VSTEP = (16 * 128) >> 4;
             bool ok = mbar_wait_spin(&s.bar_q, 0, abort, limit_ns, status, K_ENC, 20) &&
                       mbar_wait_spin(&s.bar_kf[0], 0, abort, limit_ns, status, K_ENC, 21);
             if (ok) {
                 tc_fence_after();
-                const uint32_t ka = smem_u32(s.k[0]);
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; kk++)
-                    umma_f16_ss(tS, sdesc_sw128(qa + kk * 32, 16, SBO), sdesc_sw128(ka + kk * 32, 16, SBO), IDESC_QK,
-                                kk > 0);
+                    umma_f16_ss(tS, qd + kk * KSTEP, kd0 + kk * KSTEP, IDESC_QK, kk > 0);
                 umma_commit(&s.bar_sf);
                 umma_commit(&s.bar_ke[0]);
             }
@@ -161,11 +166,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                          mbar_wait_spin(&s.bar_kf[st1], ((j + 1) / KST) & 1, abort, limit_ns, status, K_ENC, 23);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t ka = smem_u32(s.k[st1]);
+                    const uint64_t kd = kd0 + st1 * STAGE;
 #pragma unroll
                     for (int kk = 0; kk < HD / 16; kk++)
-                        umma_f16_ss(tS, sdesc_sw128(qa + kk * 32, 16, SBO), sdesc_sw128(ka + kk * 32, 16, SBO),
-                                    IDESC_QK, kk > 0);
+                        umma_f16_ss(tS, qd + kk * KSTEP, kd + kk * KSTEP, IDESC_QK, kk > 0);
                     umma_commit(&s.bar_sf);
                     umma_commit(&s.bar_ke[st1]);
                 }
@@ -174,11 +178,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                      mbar_wait_spin(&s.bar_vf[sv], (j / VST) & 1, abort, limit_ns, status, K_ENC, 25);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t va = smem_u32(s.v[sv]);
+                const uint64_t vd = vd0 + sv * STAGE;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++)
-                    umma_f16_ts(tO, tP + kk * 8, sdesc_sw128(va + kk * 16 * 128, TILE, SBO), IDESC_PV,
-                                (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16_ts(tO, tP + kk * 8, vd + kk * VSTEP, IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(&s.bar_od);
                 umma_commit(&s.bar_ve[sv]);
             }
