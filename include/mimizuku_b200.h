@@ -29,7 +29,7 @@ int mmz_init(int device);
 const char* mmz_last_error(void);
 /* Reads and clears the device status word of the current device: code[0] error (0 none, 1 wait timed out,
  * 2 misaligned shared memory, 3 bad argument), code[1] kernel (1 enc_flash, 2 self_attn, 3 cross_attn, 4 layernorm,
- * 5 dec_linear, 6 the wait self-test), code[2] site.
+ * 5 dec_linear, 6 the wait self-test, 7 logits_argmax), code[2] site.
  * Synchronises the device. No reference counterpart (the reference has no in-kernel failure detection). */
 int mmz_status(int code[3]);
 /* Sets the bound on every in-kernel wait, in milliseconds (default 1000). */
@@ -108,6 +108,24 @@ int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void
  * agree to fp32 rounding before the final fp16 rounding. */
 int mmz_dec_linear(const void* x, int ldx, const void* w, const void* bias, void* y, int ldy, int m, int n, int k,
                    int gelu, void* stream);
+
+/* The decoding step's logits fused with the greedy choice: for m <= 32 sequences, logits = rh(x . emb^T) over the
+ * vocabulary (x [m][ldx] fp16, emb [vocab][d] fp16, d a multiple of 64 up to 1280; the product of src/model.rs:714-716)
+ * and token p + 1 = argmax_tok's choice at p = ctr[0] (kernels/whisper.cu:451-493): suppressed ids (sup[id] != 0, and
+ * bs1 / bs2 at the first generated position p + 1 == prompt_len) never chosen, ties to the lower id, a finished
+ * sequence (done != 0) or one with no candidate gets eos, and eos sets done; nothing is chosen when
+ * p + 1 < prompt_len or p + 1 >= max_t. tok [m][max_t], done [m]. advance != 0 also sets ctr[0] = p + 1 (advance,
+ * kernels/whisper.cu:495). The logits are not written to memory unless `logits` ([m][vocab] fp16) is given, and then
+ * only at steps that choose a token. Replaces the logits GEMM + argmax_tok + advance launches of src/model.rs:714-735;
+ * each logit is the fp16 rounding of one fp32 accumulation in K order, as mmz_dec_linear computes it (bias NULL) when
+ * it does not split K (vocabularies of more than 128 x SM-count ids, every Whisper vocabulary on a B200), so the tokens
+ * equal argmax_tok's on mmz_dec_linear's logits there. scratch: a
+ * device buffer of mmz_logits_argmax_scratch_bytes() bytes, 16-byte aligned, zero-filled once before the first call
+ * (every call leaves it zero again); launches that share it must not overlap on the GPU. */
+unsigned long long mmz_logits_argmax_scratch_bytes(void);
+int mmz_logits_argmax(const void* x, int ldx, const void* emb, int vocab, int d, int m, const unsigned char* sup,
+                      int* tok, int* done, int* ctr, int max_t, int prompt_len, int eos, int bs1, int bs2, void* logits,
+                      int advance, void* scratch, unsigned long long scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------- token timestamps (host, src/align.rs) */
 

@@ -66,6 +66,8 @@ SIGNATURES = {
     "mmz_align_cost": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "mmz_dtw_times": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "mmz_logits_argmax_scratch_bytes": (_ULL, []),
+    "mmz_logits_argmax": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _ULL, _P]),
     "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
     "mmz_log_mel": (_I, [_FP, _L, _I, _FP, _IP]),
     "mmz_log_mel_gpu_work_bytes": (_ULL, [_I]),
@@ -242,6 +244,23 @@ def dec_linear(x, w, bias, y, gelu=False, m=None, stream=None):
     n, k = w.shape
     _check(lib.mmz_dec_linear(_ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), mm, n, k,
                               1 if gelu else 0, _stream(stream)), "dec_linear")
+
+
+def logits_argmax_scratch_bytes():
+    return lib.mmz_logits_argmax_scratch_bytes()
+
+
+def logits_argmax(x, emb, sup, tok, done, ctr, max_t, prompt_len, eos, bs=(-1, -1), scratch=None, logits=None,
+                  advance=False, m=None, stream=None):
+    """The decoding step's logits x . emb^T fused with argmax_tok's greedy choice of token ctr[0] + 1 (src/model.rs:
+    714-735): x [m][d] fp16, emb [vocab][d] fp16, sup [vocab] uint8, tok [m][max_t] int32, done [m] int32, ctr int32
+    device tensors; scratch: a zero-filled uint8 device tensor of logits_argmax_scratch_bytes() (left zero); logits
+    [m][vocab] fp16 written when given."""
+    mm = m if m is not None else x.shape[0]
+    V, d = emb.shape
+    _check(lib.mmz_logits_argmax(_ptr(x), x.stride(0), _ptr(emb), V, d, mm, _ptr(sup), _ptr(tok), _ptr(done), _ptr(ctr),
+                                 max_t, prompt_len, eos, bs[0], bs[1], _ptr(logits), 1 if advance else 0, _ptr(scratch),
+                                 scratch.numel() * scratch.element_size(), _stream(stream)), "logits_argmax")
 
 
 def align_cost(align, rows, cols, np_, max_t, na, cost, n=None, stream=None):

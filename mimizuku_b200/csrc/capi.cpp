@@ -101,6 +101,15 @@ int mmz_dec_linear(const void* x, int ldx, const void* w, const void* bias, void
     return launch_dec_linear(x, ldx, w, bias, y, ldy, m, n, k, gelu != 0, S(stream));
 }
 
+unsigned long long mmz_logits_argmax_scratch_bytes(void) { return logits_argmax_scratch_bytes(); }
+
+int mmz_logits_argmax(const void* x, int ldx, const void* emb, int vocab, int d, int m, const unsigned char* sup,
+                      int* tok, int* done, int* ctr, int max_t, int prompt_len, int eos, int bs1, int bs2, void* logits,
+                      int advance, void* scratch, unsigned long long scratch_bytes, void* stream) {
+    return launch_logits_argmax(x, ldx, emb, vocab, d, m, sup, tok, done, ctr, max_t, prompt_len, eos, bs1, bs2, logits,
+                                advance != 0, scratch, (size_t)scratch_bytes, S(stream));
+}
+
 int mmz_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int max_t, int na, void* cost,
                    void* stream) {
     return launch_align_cost(align, rows, cols, n, np, max_t, na, cost, S(stream));

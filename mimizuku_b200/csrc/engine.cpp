@@ -58,6 +58,11 @@ class Kernels {
                      cudaStream_t st) = 0;
     // the logits product hb emb^T (model.rs:714-716) where the image has a kernel for it; -2: use cuBLAS
     virtual int logits(const void*, int, const void*, void*, int, int, int, cudaStream_t) { return -2; }
+    // the logits product, argmax_tok and advance as one kernel (model.rs:714-735) where the image has one; -2: no
+    virtual int logits_argmax(const void*, int, const void*, int, int, const unsigned char*, int*, int*, int*, int,
+                              int, int, int, int, cudaStream_t) {
+        return -2;
+    }
 };
 
 // ---------------------------------------------------------------- native sm_100a kernels
@@ -123,6 +128,18 @@ class NativeKernels : public Kernels {
     int logits(const void* hb, int d, const void* emb, void* out, int vocab, int b, int, cudaStream_t st) override {
         if (b > 32) return -2;
         return ++launches, launch_dec_linear(hb, d, emb, nullptr, out, vocab, b, vocab, d, false, st);
+    }
+    // the logits streamed once and reduced to each sequence's token on the GPU, no [b][vocab] logits in memory
+    // (m <= 32, d <= 1280); lgscratch: its zero-initialised scratch, owned by the engine
+    void* lgscratch = nullptr;
+    size_t lgscratch_bytes = 0;
+    bool fused_logits = true;
+    int logits_argmax(const void* hb, int d, const void* emb, int vocab, int b, const unsigned char* sup, int* tok,
+                      int* done, int* ctr, int maxT, int prompt_len, int eos, int bs1, int bs2,
+                      cudaStream_t st) override {
+        if (!fused_logits || b > 32 || d > 1280 || !lgscratch) return -2;
+        return ++launches, launch_logits_argmax(hb, d, emb, vocab, d, b, sup, tok, done, ctr, maxT, prompt_len, eos,
+                                                bs1, bs2, nullptr, true, lgscratch, lgscratch_bytes, st);
     }
 };
 
@@ -425,6 +442,11 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         NativeKernels* nk = static_cast<NativeKernels*>(k_.get());
         nk->xscratch_bytes = cross_attn_scratch_bytes(bmax, d);
         nk->xscratch = alloc(nk->xscratch_bytes);
+        nk->lgscratch_bytes = logits_argmax_scratch_bytes();
+        nk->lgscratch = alloc(nk->lgscratch_bytes);  // zero-filled by alloc, as the fused logits kernel needs
+        // a test hook: MMZ_TEST_UNFUSED_LOGITS=1 keeps the logits product, argmax_tok and advance as three launches, so
+        // that the two paths can be compared
+        if (const char* t = getenv("MMZ_TEST_UNFUSED_LOGITS")) nk->fused_logits = t[0] != '1';
         s_ = nk->xscratch;
         stat_ = part_ = nullptr;
     }
@@ -838,6 +860,10 @@ int Engine::step(int b, int prompt_len) {
         for (int i = 0; i < nl; i++) CK(dec_layer(i, 0, b, st_, blas_));
     }
     // logits = hb emb^T (no bias), then the greedy choice and the position counter
+    const int bs1 = gc_.bs[0], bs2 = gc_.bs[1];
+    const int fr = k_->logits_argmax(hb_, d, emb_, dm_.vocab, b, sup_, tok_, done_, ctr_, mt, prompt_len, gc_.eos, bs1,
+                                     bs2, st_);
+    if (fr != -2) return fr;  // one kernel did all three (model.rs:714-735)
     const int lr = k_->logits(hb_, d, emb_, logits_, dm_.vocab, b, d, st_);
     if (lr == -1) return -1;
     if (lr == 0) {
@@ -848,7 +874,6 @@ int Engine::step(int b, int prompt_len) {
     } else {
         CK(matmul(true, false, dm_.vocab, b, d, 1.f, emb_, d, 0, hb_, d, 0, 0.f, logits_, dm_.vocab, 0, 1));
     }
-    const int bs1 = gc_.bs[0], bs2 = gc_.bs[1];
     CK(k_->argmax_tok(logits_, dm_.vocab, sup_, tok_, done_, ctr_, b, mt, prompt_len, gc_.eos, bs1, bs2, st_));
     return k_->advance(ctr_, st_);
 }

@@ -60,6 +60,7 @@ void init_dec_attn_attrs(DevCtx& c);
 int launch_wait_selftest(int limit_ms, cudaStream_t st);
 void init_enc_attn_attrs();
 void init_dec_linear_attrs();
+void init_logits_argmax_attrs();
 void init_align_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
@@ -80,6 +81,14 @@ int launch_add_layernorm(void* x, const void* d, const void* w, const void* b, v
 // (dec_linear.cu)
 int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, void* y, int ldy, int m, int n, int k,
                       bool gelu, cudaStream_t st);
+
+// logits of m <= 32 sequences (x [m][ldx], emb [V][k], k <= 1280) fused with argmax_tok's choice of token ctr[0] + 1
+// (and ctr[0] += 1 when advance); logits [m][V] fp16 written only when not null; scratch of
+// logits_argmax_scratch_bytes(), zero before the first launch and left zero by every launch (logits_argmax.cu)
+size_t logits_argmax_scratch_bytes();
+int launch_logits_argmax(const void* x, int ldx, const void* emb, int V, int k, int m, const unsigned char* sup,
+                         int* tok, int* done, int* ctr, int maxT, int prompt_len, int eos, int bs1, int bs2,
+                         void* logits, bool advance, void* scratch, size_t scratch_bytes, cudaStream_t st);
 
 // the DTW cost of the token timestamps for a batch of clips (align.cu)
 int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,

@@ -71,6 +71,7 @@ static void init_ctx(DevCtx& c, int dev) {
     init_dec_attn_attrs(c);
     init_enc_attn_attrs();
     init_dec_linear_attrs();
+    init_logits_argmax_attrs();
     init_align_attrs();
     cudaGetLastError();
     c.ok = true;

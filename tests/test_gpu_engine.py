@@ -271,3 +271,26 @@ def test_lane_check_failure_falls_back_to_one_lane(cuda, monkeypatch):
     ok.close()
     for k in ("tokens", "lens", "times"):
         assert np.array_equal(r[k], x[k]), k
+
+
+@pytest.mark.parametrize("b", [32, 5])
+def test_fused_logits_argmax_matches_three_launches(cuda, monkeypatch, b):
+    """The native step's fused logits + greedy choice + advance (one kernel) gives exactly the tokens, lengths and
+    times of the logits kernel, argmax_tok and advance launched one after the other (the library's test hook keeps
+    that path), in the captured graph and eagerly."""
+    import mimizuku_b200 as m
+    cfg = m.TINY
+    mel, frames = _clips(b, cfg.n_mels, seed=9)
+    out = {}
+    for unfused in (False, True):
+        if unfused:
+            monkeypatch.setenv("MMZ_TEST_UNFUSED_LOGITS", "1")
+        e = m.Engine(cfg, bmax=b, eg=8, seed=3, suppress=[cfg.eos])
+        monkeypatch.delenv("MMZ_TEST_UNFUSED_LOGITS", raising=False)
+        for graph in (True, False):
+            out[unfused, graph] = e.transcribe(mel, frames, max_new=20, graph=graph)
+        e.close()
+    for key in out:
+        for k in ("tokens", "lens", "times"):
+            assert np.array_equal(out[key][k], out[True, True][k]), (key, k)
+    assert (out[False, True]["lens"] == len(cfg.prompt) + 20).all()
