@@ -101,6 +101,12 @@ int mmz_layernorm(const void* x, const void* w, const void* b, void* out, int ro
 int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
                       void* stream);
 
+/* Row softmax in place: each of `rows` rows of n <= 2048 fp16 values becomes rh(exp(s - max) / sum) (fp32 inside);
+ * rows 8-byte aligned (n a multiple of 4 when rows > 1). Replaces softmax_rows (kernels/whisper.cu:141-166), which
+ * the unfused encoder attention launches (src/model.rs:588); its sum associates differently, so a probability may
+ * differ from the reference kernel's in the last fp16 bit. */
+int mmz_softmax_rows(void* s, long rows, int n, void* stream);
+
 /* Decoder linear layer at m <= 32 sequences: y[m][n] = rh(x[m][:k] . w[n][:k] + bias[n]) (fp16 in and out, fp32
  * accumulation; bias may be NULL), then GELU when gelu != 0 (fc1 followed by gelu_inplace, kernels/whisper.cu:107-112). x [m][ldx],
  * w [n][k], y [m][ldy]; k a multiple of 64, x and w 16-byte aligned. Replaces the decoder step's cuBLAS GEMMs onto
@@ -231,6 +237,14 @@ int mmz_engine_replay(mmz_engine* e);
  * only 1. Takes effect at the next step or capture. */
 int mmz_engine_set_lanes(mmz_engine* e, int lanes);
 int mmz_engine_lanes(mmz_engine* e);
+/* Encoder attention of the engine: 0 (the default) the image's fused kernel (this library's mmz_enc_flash, or the
+ * reference's enc_flash on a fatbin image); 1 the unfused comparison path of src/model.rs:567-604 (--enc-attn cublas,
+ * src/main.rs:37, 179): per clip the scores 0.125 K Q^T of every head into a [heads][1500][1500] fp16 buffer (one
+ * cuBLAS strided-batched GEMM; the buffer, 90 MB for 20 heads, is allocated at the first encode in this mode), the row
+ * softmax in place (this library's kernel, or the reference's softmax_rows on a fatbin image), then P.V (cuBLAS).
+ * Takes effect at the next encode. */
+int mmz_engine_set_enc_attn(mmz_engine* e, int unfused);
+int mmz_engine_enc_attn(mmz_engine* e);
 /* Device address of an engine buffer: "tok", "done", "ctr", "align", "logits", "eh", "eqkv", "eatt", "xkv", "mel",
  * "kc", "vc", "x", "hb", "att", "aslot"; NULL if unknown. */
 void* mmz_engine_buffer(mmz_engine* e, const char* name);

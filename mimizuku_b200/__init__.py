@@ -66,6 +66,7 @@ SIGNATURES = {
     "mmz_align_cost": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "mmz_dtw_times": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
+    "mmz_softmax_rows": (_I, [_P, _L, _I, _P]),
     "mmz_logits_argmax_scratch_bytes": (_ULL, []),
     "mmz_logits_argmax": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _ULL, _P]),
     "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
@@ -87,6 +88,8 @@ SIGNATURES = {
     "mmz_engine_replay": (_I, [_P]),
     "mmz_engine_set_lanes": (_I, [_P, _I]),
     "mmz_engine_lanes": (_I, [_P]),
+    "mmz_engine_set_enc_attn": (_I, [_P, _I]),
+    "mmz_engine_enc_attn": (_I, [_P]),
     "mmz_engine_buffer": (_P, [_P, ctypes.c_char_p]),
     "mmz_engine_stream": (_P, [_P]),
     "mmz_engine_sync": (_I, [_P]),
@@ -244,6 +247,13 @@ def dec_linear(x, w, bias, y, gelu=False, m=None, stream=None):
     n, k = w.shape
     _check(lib.mmz_dec_linear(_ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), mm, n, k,
                               1 if gelu else 0, _stream(stream)), "dec_linear")
+
+
+def softmax_rows(s, n=None, rows=None, stream=None):
+    """Row softmax in place of an fp16 device tensor [rows][n] (kernels/whisper.cu:141-166)."""
+    n = n if n is not None else s.shape[-1]
+    rows = rows if rows is not None else s.numel() // n
+    _check(lib.mmz_softmax_rows(_ptr(s), rows, n, _stream(stream)), "softmax_rows")
 
 
 def logits_argmax_scratch_bytes():

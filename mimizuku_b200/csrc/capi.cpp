@@ -101,6 +101,8 @@ int mmz_dec_linear(const void* x, int ldx, const void* w, const void* bias, void
     return launch_dec_linear(x, ldx, w, bias, y, ldy, m, n, k, gelu != 0, S(stream));
 }
 
+int mmz_softmax_rows(void* s, long rows, int n, void* stream) { return launch_softmax_rows(s, rows, n, S(stream)); }
+
 unsigned long long mmz_logits_argmax_scratch_bytes(void) { return logits_argmax_scratch_bytes(); }
 
 int mmz_logits_argmax(const void* x, int ldx, const void* emb, int vocab, int d, int m, const unsigned char* sup,
@@ -227,6 +229,8 @@ int mmz_engine_capture(mmz_engine* e, int b, int prompt_len) {
 int mmz_engine_replay(mmz_engine* e) { return e ? e->e->replay() : fail("null engine"); }
 int mmz_engine_set_lanes(mmz_engine* e, int lanes) { return e ? e->e->set_lanes(lanes) : fail("null engine"); }
 int mmz_engine_lanes(mmz_engine* e) { return e ? e->e->lanes() : 0; }
+int mmz_engine_set_enc_attn(mmz_engine* e, int unfused) { return e ? e->e->set_enc_attn(unfused) : fail("null engine"); }
+int mmz_engine_enc_attn(mmz_engine* e) { return e ? e->e->enc_attn() : -1; }
 void* mmz_engine_buffer(mmz_engine* e, const char* name) { return e && name ? e->e->buffer(name) : nullptr; }
 void* mmz_engine_stream(mmz_engine* e) { return e ? (void*)e->e->stream() : nullptr; }
 int mmz_engine_sync(mmz_engine* e) {

@@ -37,6 +37,8 @@ class Kernels {
     virtual int layernorm(const void* x, const Ln& l, void* y, int rows, int d, cudaStream_t st) = 0;
     virtual int add_layernorm(void* x, const void* dx, const Ln& l, void* y, int rows, int d, cudaStream_t st) = 0;
     virtual int enc_attn(const void* qkv, void* out, int gn, int d, int nh, cudaStream_t st) = 0;
+    // row softmax in place of the unfused encoder attention (kernels/whisper.cu:141-166)
+    virtual int softmax_rows(void* s, long rows, int n, cudaStream_t st) = 0;
     virtual int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b,
                           int maxT, int d, int nh, cudaStream_t st) = 0;
     virtual int cross_attn(const void* xq, const void* kv, void* s, void* stat, void* part, void* att, void* align,
@@ -80,6 +82,9 @@ class NativeKernels : public Kernels {
     }
     int enc_attn(const void* qkv, void* out, int gn, int d, int, cudaStream_t st) override {
         return ++launches, launch_enc_flash(qkv, out, gn, d, st);
+    }
+    int softmax_rows(void* s, long rows, int n, cudaStream_t st) override {
+        return ++launches, launch_softmax_rows(s, rows, n, st);
     }
     // kv_write is folded into the self-attention kernel
     int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b, int maxT,
@@ -243,6 +248,10 @@ class FatbinKernels : public Kernels {
     // model.rs:566
     int enc_attn(const void* qkv, void* out, int gn, int d, int nh, cudaStream_t st) override {
         return k("enc_flash", (TENC_ + 63) / 64, nh, gn, 128, 0, st, {Arg::P(qkv), Arg::P(out), Arg::I(d)});
+    }
+    // model.rs:588
+    int softmax_rows(void* s, long rows, int n, cudaStream_t st) override {
+        return k("softmax_rows", (unsigned)rows, 1, 1, 256, 0, st, {Arg::P(s), Arg::I(n)});
     }
     // model.rs:665-672
     int self_attn(const void* qkv, void* kc, void* vc, void* att, const int* ctr, const int* done, int b, int maxT,
@@ -752,7 +761,8 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     for (size_t i = 0; i < enc_.size(); i++) {
         const EncLayer& l = enc_[i];
         CK(lin_enc(eh_, d, l.qkv, eqkv_, 3 * d, r2, 3 * d, d));
-        CK(k_->enc_attn(eqkv_, eatt_, gn, d, nh, st_));
+        if (enc_unfused_) CK(enc_attn_unfused(gn));
+        else CK(k_->enc_attn(eqkv_, eatt_, gn, d, nh, st_));
         CK(lin_enc(eatt_, d, l.o, eh_, d, r2, d, d));
         CK(k_->add_layernorm(ex_, eh_, l.ln2, eh_, r2, d, st_));
         CK(lin_enc(eh_, d, l.fc1, ef_, ff, r2, ff, d));
@@ -775,6 +785,35 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
         CK(matmul(true, false, HDIM, TENC_, d, 1.f, xkv_.w, d, (long long)HDIM * d, xc, d, 0, 1.f, dst, HDIM,
                   (long long)TENC_ * HDIM, nblk));
     }
+    return 0;
+}
+
+// The unfused encoder attention of model.rs:567-604 (--enc-attn cublas), clip by clip: scores^T = 0.125 K Q^T per head
+// into the [heads][query][key] fp16 buffer esc (one strided-batched GEMM), the row softmax in place, then
+// att = (V^T P^T)^T (one more), with the reference's GEMM parameters.
+int Engine::enc_attn_unfused(int gn) {
+    const int d = dm_.d, nh = dm_.nh;
+    if (!esc_) {
+        esc_ = alloc((size_t)nh * TENC_ * TENC_ * 2);
+        if (!esc_) return fail("enc_attn (cublas): device memory allocation failed");
+    }
+    for (int c = 0; c < gn; c++) {
+        const char* q = (const char*)eqkv_ + 2 * (size_t)c * TENC_ * 3 * d;
+        const char* kk = q + 2 * (size_t)d;
+        const char* v = q + 4 * (size_t)d;
+        CK(matmul(true, false, TENC_, TENC_, HDIM, 0.125f, kk, 3 * d, HDIM, q, 3 * d, HDIM, 0.f, esc_, TENC_,
+                  (long long)TENC_ * TENC_, nh));
+        CK(k_->softmax_rows(esc_, (long)nh * TENC_, TENC_, st_));
+        void* out = (char*)eatt_ + 2 * (size_t)c * TENC_ * d;
+        CK(matmul(false, false, HDIM, TENC_, TENC_, 1.f, v, 3 * d, HDIM, esc_, TENC_, (long long)TENC_ * TENC_, 0.f,
+                  out, d, HDIM, nh));
+    }
+    return 0;
+}
+
+int Engine::set_enc_attn(int unfused) {
+    if (unfused != 0 && unfused != 1) return fail("set_enc_attn: 0 (fused kernel) or 1 (cuBLAS scores, row softmax, cuBLAS P.V)");
+    enc_unfused_ = unfused == 1;
     return 0;
 }
 

@@ -91,6 +91,10 @@ class Engine {
     // (lanes_rows_match; 1 lane if not); other batch sizes use one lane. The fatbin image always uses 1.
     int set_lanes(int n);
     int lanes() const { return lanes_; }
+    // encoder attention: 0 the image's fused kernel (enc_flash), 1 the unfused comparison path of model.rs:567-604
+    // (cuBLAS scores into a [heads][1500][1500] buffer, row softmax, cuBLAS P.V; --enc-attn cublas, main.rs:37, 179)
+    int set_enc_attn(int unfused);
+    int enc_attn() const { return enc_unfused_ ? 1 : 0; }
 
    private:
     int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
@@ -109,6 +113,7 @@ class Engine {
     // decoder layer i (model.rs:665-705) for the sequences [r0, r0 + bh) on stream st with cuBLAS handle h
     int dec_layer(int i, int r0, int bh, cudaStream_t st, cublasHandle_t h);
     int lanes_rows_match();
+    int enc_attn_unfused(int gn);
     void* alloc(size_t bytes);
     int decode_and_times(const int* frames, int n, const int* prompt, int np, int max_steps, bool graph, int threads,
                          int* tokens, int* lens, float* times, double* stage_s,
@@ -124,6 +129,8 @@ class Engine {
     cudaStream_t st_ = nullptr;
     cublasHandle_t blas_ = nullptr;
     int lanes_ = 1;
+    bool enc_unfused_ = false;
+    void* esc_ = nullptr;  // the unfused encoder attention's scores, allocated on first use
     bool lanes_ok_ = false;          // lanes_rows_match() found the half-batch rows equal
     cudaStream_t st2_ = nullptr;     // second decoder lane
     cublasHandle_t blas2_ = nullptr;

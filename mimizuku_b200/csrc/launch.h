@@ -104,6 +104,8 @@ int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe
 int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
                       int batch, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st);
 int launch_advance(int* ctr, cudaStream_t st);
+// row softmax in place, rows of n <= 2048 fp16 values (8-byte aligned rows): the unfused encoder attention's
+int launch_softmax_rows(void* s, long rows, int n, cudaStream_t st);
 int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st);
 int launch_im2col2(const void* h1, void* X, long n, int d, cudaStream_t st);
 int launch_gelu(void* x, long n, cudaStream_t st);

@@ -205,6 +205,72 @@ int launch_embed(const int* tok, const int* ctr, const void* emb, const void* pe
                      "embed");
 }
 
+// Row softmax in place for the unfused encoder attention (kernels/whisper.cu:141-166, launched by src/model.rs:588):
+// each fp16 row of n <= 2048 scores becomes rh(exp(s - max) / sum) with fp32 arithmetic inside. One warp per row,
+// eight rows per CTA, 8-byte loads and stores (rows of a multiple of 4 values start 8-byte aligned); the maximum and
+// the sum are warp shuffles, so no barrier is taken. The sum associates differently from the reference kernel's
+// 256-thread tree, so a probability may differ from it in the last fp16 bit.
+constexpr int SM_VEC = 16;  // 4-value vectors per lane: n <= 32 * 4 * 16 = 2048
+__global__ void __launch_bounds__(256) softmax_rows_kernel(h16* __restrict__ s, long rows, int n) {
+    griddep_wait();  // launched as a programmatic dependent of the scores product
+    const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    h16* r = s + row * n;
+    const int nv = n >> 2;  // whole vectors; n % 4 values follow
+    float v[SM_VEC][4];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < SM_VEC; k++) {
+        const int i = lane + 32 * k;
+        if (i < nv) {
+            const uint2 u = reinterpret_cast<const uint2*>(r)[i];
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+            v[k][0] = a.x, v[k][1] = a.y, v[k][2] = b.x, v[k][3] = b.y;
+        } else {
+            v[k][0] = v[k][1] = v[k][2] = v[k][3] = -INFINITY;
+        }
+        m = fmaxf(m, fmaxf(fmaxf(v[k][0], v[k][1]), fmaxf(v[k][2], v[k][3])));
+    }
+    const int tail = n - 4 * nv;  // at most 3 values, taken by lanes 0..2
+    float tv = lane < tail ? f(r[4 * nv + lane]) : -INFINITY;
+    m = fmaxf(m, tv);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffff, m, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < SM_VEC; k++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            v[k][e] = v[k][e] == -INFINITY ? 0.f : expf(v[k][e] - m);
+            sum += v[k][e];
+        }
+    tv = tv == -INFINITY ? 0.f : expf(tv - m);
+    sum += tv;
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int k = 0; k < SM_VEC; k++) {
+        const int i = lane + 32 * k;
+        if (i < nv) {
+            const __half2 a = __floats2half2_rn(v[k][0] * inv, v[k][1] * inv);
+            const __half2 b = __floats2half2_rn(v[k][2] * inv, v[k][3] * inv);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&a);
+            u.y = *reinterpret_cast<const uint32_t*>(&b);
+            reinterpret_cast<uint2*>(r)[i] = u;
+        }
+    }
+    if (lane < tail) r[4 * nv + lane] = h(tv * inv);
+}
+
+int launch_softmax_rows(void* s, long rows, int n, cudaStream_t st) {
+    if (rows < 1 || n < 1 || n > 32 * 4 * SM_VEC) return fail("softmax_rows: 1 <= n <= 2048");
+    if (((uintptr_t)s & 7) || (n % 4 && rows > 1)) return fail("softmax_rows: rows must start 8-byte aligned");
+    return check_pdl(launch_pdl(softmax_rows_kernel, dim3(blocks(rows, 8)), dim3(256), 0, st, (h16*)s, rows, n),
+                     "softmax_rows");
+}
+
 int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* tok, int* done, const int* ctr,
                       int batch, int maxT, int prompt_len, int eos, int bs1, int bs2, cudaStream_t st) {
     return check_pdl(launch_pdl(argmax_kernel, dim3(batch), dim3(1024), 0, st, (const h16*)logits, V, sup, tok, done,

@@ -159,6 +159,18 @@ class Engine:
     def lanes(self, n):
         _check(lib.mmz_engine_set_lanes(self._h, int(n)), "set_lanes")
 
+    @property
+    def enc_attn(self):
+        """Encoder attention: "flash" (the default: the kernel image's fused attention) or "cublas" (the unfused
+        comparison path of src/model.rs:567-604: cuBLAS scores, row softmax, cuBLAS P.V)."""
+        return "cublas" if lib.mmz_engine_enc_attn(self._h) == 1 else "flash"
+
+    @enc_attn.setter
+    def enc_attn(self, mode):
+        if mode not in ("flash", "cublas"):
+            raise MmzError("enc_attn: 'flash' or 'cublas'")
+        _check(lib.mmz_engine_set_enc_attn(self._h, 1 if mode == "cublas" else 0), "set_enc_attn")
+
     def buffer(self, name):
         p = lib.mmz_engine_buffer(self._h, name.encode())
         if not p:
