@@ -29,7 +29,7 @@ def f16(t):
 # ------------------------------------------------------------------ layer norm
 
 @pytest.mark.parametrize("rows,dim", [(1, 384), (3, 1280), (32, 1280), (12000, 1280), (7, 512), (5, 768),
-                                      (2049, 384), (1030, 640)])
+                                      (2049, 384), (1030, 640), (1100, 1278)])
 def test_layernorm_matches_reference_bit_for_bit(cuda, ref, rows, dim):
     import mimizuku_b200 as m
     torch = cuda
