@@ -76,7 +76,10 @@ int mmz_kv_write(const void* qkv, void* kc, void* vc, const int* ctr, int batch,
  * (sequence, head). Replaces cross_scores + cross_pv + cross_combine (kernels/whisper.cu:368, :407, :443;
  * src/model.rs:676-705), whose S / stat / part buffers (model.rs:452-454) become `scratch`: a device buffer of at
  * least mmz_cross_attn_scratch_bytes(batch, d) bytes, 16-byte aligned, with no initial contents required.
- * Launches that share a scratch buffer must not overlap on the GPU. kv 16-byte aligned. */
+ * Launches that share a scratch buffer must not overlap on the GPU. kv 16-byte aligned. Launched as a programmatic
+ * dependent of the kernel before it on the stream: kv and done are read before that kernel has finished (in the
+ * reference's decoding step they come from the encoder and from earlier steps), so they must not be written by the
+ * kernel immediately before this call; q may be. */
 int mmz_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
                    const int* done, int batch, int layer, int nl, int d, int na, int max_t, void* scratch,
                    unsigned long long scratch_bytes, void* stream);

@@ -280,7 +280,8 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     return v;
 }
 
-// grid (8, heads, B), block 128. Every thread's twelve 16-byte K loads are issued before any is used.
+// grid (8, heads, B), block 128. Every thread's twelve 16-byte K loads are issued before any is used, and before the
+// wait for the kernel before (the q projection): K comes from the encoder and done from earlier decoding steps.
 __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict__ q, const h16* __restrict__ kv,
                                                            XScratch xs, const int* __restrict__ done, int layer,
                                                            int nl, int d) {
@@ -288,7 +289,6 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
     __shared__ float qs[HD];
     __shared__ float sc[XPER];
     griddep_launch_dependents();  // the P.V kernel may start its V copies as soon as every CTA here is resident
-    griddep_wait();               // launched as a programmatic dependent of the q projection
     const int b = blockIdx.z, hh = blockIdx.y, r = blockIdx.x, t = threadIdx.x;
     const int nh = d / HD, bh = b * nh + hh;
     if (done[b]) return;
@@ -301,6 +301,7 @@ __global__ void __launch_bounds__(128) cross_scores_kernel(const h16* __restrict
         const int jj = grp + 16 * i;
         u[i] = jj < n ? ldg_stream(K + jj * HD) : make_uint4(0, 0, 0, 0);
     }
+    griddep_wait();  // q comes from the kernel before; K and done from the encoder and earlier steps
     if (t < HD) qs[t] = rh(f(q[(long)b * d + hh * HD + t]) * 0.125f);
     __syncthreads();
     // scores: a group of 8 lanes per position (kernels/whisper.cu:376-392)

@@ -115,15 +115,17 @@ __global__ void __launch_bounds__(128) dec_linear_splitk_kernel(const __grid_con
                 mbar_wait(&s.full[i % NS], (i / NS) & 1, nullptr, limit_ns, nullptr, 0, 0);
     } else if (threadIdx.x == 32) {
         // ------------------------------------------------------------ MMA issuer
+        // descriptors formed once and advanced by constants (a stage, a K step only move the start address field)
+        const uint64_t wd0 = sdesc_sw128(smem_u32(s.w[0]), 16, 1024), xd0 = sdesc_sw128(smem_u32(s.x[0]), 16, 1024);
+        constexpr uint64_t WSTAGE = WT >> 4, XSTAGE = XT >> 4, KSTEP = 32 >> 4;
         for (int c = c0; c < c1; c++) {
             const int i = c - c0, st = i % NS;
             if (!mbar_wait_spin(&s.full[st], (i / NS) & 1, abort, limit_ns, status, K_LIN, 2)) break;
             tc_fence_after();
-            const uint32_t wa = smem_u32(s.w[st]), xa = smem_u32(s.x[st]);
+            const uint64_t wd = wd0 + st * WSTAGE, xd = xd0 + st * XSTAGE;
 #pragma unroll
             for (int kk = 0; kk < BK / 16; kk++)
-                umma_f16_ss(tacc, sdesc_sw128(wa + kk * 32, 16, 1024), sdesc_sw128(xa + kk * 32, 16, 1024), IDESC,
-                            (c > c0 || kk > 0) ? 1u : 0u);
+                umma_f16_ss(tacc, wd + kk * KSTEP, xd + kk * KSTEP, IDESC, (c > c0 || kk > 0) ? 1u : 0u);
             umma_commit(&s.empty[st]);
         }
         umma_commit(&s.done);  // completes when every MMA above has finished (at once if there were none)

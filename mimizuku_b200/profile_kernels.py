@@ -7,6 +7,10 @@
     python -m mimizuku_b200.profile_kernels step [n]       n decoding steps (default 4) of the large-v3 engine at batch
                                                            32 from one captured graph, inside the NVTX range "steps"
                                                            (ncu --nvtx --nvtx-include "steps/" captures only those)
+    python -m mimizuku_b200.profile_kernels logits         logits fused with the greedy choice, large-v3, batch 32
+    python -m mimizuku_b200.profile_kernels ln             add_layernorm at the encoder's 12000 x 1280
+    python -m mimizuku_b200.profile_kernels logmel         the GPU log-mel of 32 synthetic 30 s clips (128 mel bins)
+    python -m mimizuku_b200.profile_kernels align          timestamp cost and DTW of 32 clips x 223 tokens x 10 heads
 """
 import sys
 
@@ -68,6 +72,42 @@ def main(argv):
         e.sync()
         torch.cuda.nvtx.range_pop()
         e.close()
+    elif which == "logits":
+        V, d, B, mt = 51866, 1280, 32, 448
+        emb = (torch.randn(V, d, device="cuda") * 0.02).half()
+        x = torch.randn(B, d, device="cuda").half()
+        sup = torch.zeros(V, dtype=torch.uint8, device="cuda")
+        tok = torch.zeros(B, mt, dtype=torch.int32, device="cuda")
+        done = torch.zeros(B, dtype=torch.int32, device="cuda")
+        ctr = torch.tensor([100, 0, 0, 0], dtype=torch.int32, device="cuda")
+        scratch = torch.zeros(m.logits_argmax_scratch_bytes(), dtype=torch.uint8, device="cuda")
+        for _ in range(4):
+            m.logits_argmax(x, emb, sup, tok, done, ctr, mt, 4, 50257, scratch=scratch)
+    elif which == "ln":
+        R, D = 12000, 1280
+        x = torch.randn(R, D, device="cuda").half()
+        dx = torch.randn(R, D, device="cuda").half()
+        w, b = torch.randn(D, device="cuda").half(), torch.randn(D, device="cuda").half()
+        for _ in range(4):
+            m.add_layernorm(x, dx, w, b, dx)
+    elif which == "logmel":
+        n = 32
+        ys = [torch.from_numpy(m.synth_clip(1000003 * i + 17)) for i in range(n)]
+        audio = torch.stack(ys).cuda()
+        lens = torch.full((n,), 480000, dtype=torch.int32, device="cuda")
+        out = torch.empty(n, 128, 3000, device="cuda")
+        work = torch.empty(m.log_mel_gpu_work_bytes(n), dtype=torch.uint8, device="cuda")
+        for _ in range(4):
+            m.log_mel_gpu(audio, lens, 128, out, work=work)
+    elif which == "align":
+        n, mt, na, np_, rows = 32, 448, 10, 4, 223
+        align = torch.rand(n, mt, na, 1500, device="cuda").half()
+        rc = torch.tensor([rows] * n + [1500] * n, dtype=torch.int32, device="cuda")
+        cost = torch.empty(n, mt, 1500, device="cuda")
+        times = torch.empty(n, mt, device="cuda")
+        for _ in range(4):
+            m.align_cost(align, rc[:n], rc[n:], np_, mt, na, cost, n=n)
+            m.dtw_times(cost, rc[:n], rc[n:], mt, times, n=n)
     else:
         raise SystemExit(__doc__)
     torch.cuda.synchronize()
