@@ -30,10 +30,12 @@ constexpr uint32_t IDESC = idesc_f16_f32(BN, BM, false);
 
 constexpr int RP = BM + 1;    // padded partial row: conflict-free stores by row and reads by row
 
+// this CTA's partial tile, [owner rank][row of its slice][batch row], lives in the W ring once every MMA that read the
+// ring has completed: 97 KB of shared memory, so two CTAs fit an SM
+static_assert(BN * RP * 4 <= NS * WT, "the partial tile fits in the W ring");
 struct Smem {
     uint8_t w[NS][WT];
     uint8_t x[NS][XT];
-    float send[BN * RP];       // this CTA's partial tile as [owner rank][row of its slice][batch row]
     float recv[BN * RP];       // [source rank][row of this rank's slice][batch row]
     uint64_t full[NS], empty[NS], done, got;
     uint32_t tmem;
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(128) dec_linear_splitk_kernel(const __grid_con
         uint32_t v[32];
         tmem_ld32(tacc + ((uint32_t)(warp * 32) << 16), v);  // lane = W row, column = batch row
         const int row = warp * 32 + lane;
-        float* dst = &s.send[row * RP];  // [row / R][row % R][j] = [row][j]
+        float* dst = reinterpret_cast<float*>(s.w[0]) + row * RP;  // [row / R][row % R][j] = [row][j]
 #pragma unroll
         for (int j = 0; j < BM; j++) dst[j] = c1 > c0 ? __uint_as_float(v[j]) : 0.f;
         fence_proxy_async_smem();  // the bulk copies read these stores through the async proxy
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(128) dec_linear_splitk_kernel(const __grid_con
     __syncthreads();
     if (threadIdx.x == 0 && ok)
         for (int q = 0; q < S; q++)
-            bulk_s2s_cluster(dsmem_addr(&s.recv[r * R * RP], q), smem_u32(&s.send[q * R * RP]), slice_bytes,
+            bulk_s2s_cluster(dsmem_addr(&s.recv[r * R * RP], q), smem_u32(reinterpret_cast<float*>(s.w[0]) + q * R * RP), slice_bytes,
                              dsmem_addr(&s.got, q));
     // waits even after an earlier failure, so that no copy into this CTA is still in flight when it leaves
     ok = __syncthreads_and(mbar_wait_cluster(&s.got, 0, nullptr, limit_ns, status, K_LIN, 4) && ok);
@@ -189,10 +191,11 @@ int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, v
     const uint32_t xb[2] = {BK, BM};
     if (make_tmap_2d(&wm, w, wd, ws, wb, true) || make_tmap_2d(&xm, x, xd, xs, xb, true))
         return fail("dec_linear: cuTensorMapEncodeTiled failed");
-    // split K over a cluster of S CTAs: at least 2 chunks each, at most two CTAs per SM in all, 16 per cluster
+    // split K over a cluster of S CTAs (a power of two up to 16, at least one chunk each) so that the launch has up to
+    // two CTAs per SM: at m <= 32 the product is a stream over W, and more CTAs keep more of it in flight
     const int tiles = (n + BN - 1) / BN, nch = k / BK;
     int S = 1;
-    while (S < 16 && S * 4 <= nch && tiles * S * 2 <= 2 * dc.sms) S *= 2;
+    while (S < 16 && S * 2 <= nch && tiles * S * 2 <= 2 * dc.sms) S *= 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S, tiles, 1);
     cfg.blockDim = dim3(128, 1, 1);
