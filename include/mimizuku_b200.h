@@ -29,7 +29,7 @@ int mmz_init(int device);
 const char* mmz_last_error(void);
 /* Reads and clears the device status word of the current device: code[0] error (0 none, 1 wait timed out,
  * 2 misaligned shared memory, 3 bad argument), code[1] kernel (1 enc_flash, 2 self_attn, 3 cross_attn, 4 layernorm,
- * 5 dec_linear, 6 the wait self-test, 7 logits_argmax), code[2] site.
+ * 5 dec_linear, 6 the wait self-test, 7 logits_argmax, 8 gemm_bias), code[2] site.
  * Synchronises the device. No reference counterpart (the reference has no in-kernel failure detection). */
 int mmz_status(int code[3]);
 /* Sets the bound on every in-kernel wait, in milliseconds (default 1000). */
@@ -103,6 +103,17 @@ int mmz_layernorm(const void* x, const void* w, const void* b, void* out, int ro
  * src/model.rs:533-537). */
 int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void* out, int rows, int dim, float eps,
                       void* stream);
+
+/* The encoder's linear layers and cross-K/V projection on the tensor cores: C = rh(A W^T + bias) (A [m][lda] fp16,
+ * W [n][k] fp16, bias [n] fp16 or NULL, fp32 accumulation, the bias added in fp32 before the one rounding), with the
+ * work around the product in its epilogue: mode 0 stores C [m][ldc]; mode 1 applies the exact-erf GELU to the
+ * rounded value first (lin + gelu_inplace, kernels/whisper.cu:107-112); mode 2 stores C[i][j] at
+ * c + (j / 64) * blk + i * 64 + j % 64, the decoder's head-contiguous cross k/v layout ([layer][k|v][head][1500][64]
+ * with blk = 1500 * 64: model.rs:614-623 and fill_bias_heads, whisper.cu:99-104). n a multiple of 128, k of 64,
+ * 16-byte aligned operands and row pitches. Replaces the encoder's cuBLAS GEMMs onto bias images (src/gpu.rs:208-236);
+ * the summation order differs from cuBLAS's, so results agree to fp32 rounding before the final fp16 rounding. */
+int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void* c, long long ldc, int m, int n, int k,
+                  int mode, long long blk, void* stream);
 
 /* Row softmax in place: each of `rows` rows of n <= 2048 fp16 values becomes rh(exp(s - max) / sum) (fp32 inside);
  * rows 8-byte aligned (n a multiple of 4 when rows > 1). Replaces softmax_rows (kernels/whisper.cu:141-166), which

@@ -67,6 +67,7 @@ SIGNATURES = {
     "mmz_dtw_times": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "mmz_softmax_rows": (_I, [_P, _L, _I, _P]),
+    "mmz_gemm_bias": (_I, [_P, _I, _P, _P, _P, _LL, _I, _I, _I, _I, _LL, _P]),
     "mmz_logits_argmax_scratch_bytes": (_ULL, []),
     "mmz_logits_argmax": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _ULL, _P]),
     "mmz_times_from_cost": (_I, [_FP, _I, _I, _I, _FP]),
@@ -247,6 +248,16 @@ def dec_linear(x, w, bias, y, gelu=False, m=None, stream=None):
     n, k = w.shape
     _check(lib.mmz_dec_linear(_ptr(x), x.stride(0), _ptr(w), _ptr(bias), _ptr(y), y.stride(0), mm, n, k,
                               1 if gelu else 0, _stream(stream)), "dec_linear")
+
+
+def gemm_bias(a, w, bias, c, mode=0, blk=0, m=None, ldc=None, stream=None):
+    """c = rh(a w^T + bias) on the tensor cores (mode 1: then GELU; mode 2: head-blocked store, blk elements per
+    64-column block): a [m][k], w [n][k], bias [n] fp16 device tensors."""
+    mm = m if m is not None else a.shape[0]
+    n, k = w.shape
+    ld = ldc if ldc is not None else (c.stride(0) if mode != 2 else 0)
+    _check(lib.mmz_gemm_bias(_ptr(a), a.stride(0), _ptr(w), _ptr(bias), _ptr(c), ld, mm, n, k, mode, blk,
+                             _stream(stream)), "gemm_bias")
 
 
 def softmax_rows(s, n=None, rows=None, stream=None):

@@ -24,7 +24,7 @@ NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-
                      "--expt-relaxed-constexpr"]
 CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-function", f"-I{CUDA}/include"]
 
-CU = ["runtime.cu", "dec_attn.cu", "enc_attn.cu", "ln.cu", "misc.cu", "cross_noalloc.cu", "align.cu", "dec_linear.cu", "logmel.cu", "logits_argmax.cu"]
+CU = ["runtime.cu", "dec_attn.cu", "enc_attn.cu", "ln.cu", "misc.cu", "cross_noalloc.cu", "align.cu", "dec_linear.cu", "logmel.cu", "logits_argmax.cu", "gemm.cu"]
 CPP = ["host_cpu.cpp", "engine.cpp", "capi.cpp"]
 HEADERS = ["common.cuh", "launch.h", "engine.h", "host_cpu.h"]
 

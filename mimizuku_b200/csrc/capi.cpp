@@ -101,6 +101,11 @@ int mmz_dec_linear(const void* x, int ldx, const void* w, const void* bias, void
     return launch_dec_linear(x, ldx, w, bias, y, ldy, m, n, k, gelu != 0, S(stream));
 }
 
+int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void* c, long long ldc, int m, int n, int k,
+                  int mode, long long blk, void* stream) {
+    return launch_gemm_bias(a, lda, w, bias, c, (long)ldc, m, n, k, mode, (long)blk, S(stream));
+}
+
 int mmz_softmax_rows(void* s, long rows, int n, void* stream) { return launch_softmax_rows(s, rows, n, S(stream)); }
 
 unsigned long long mmz_logits_argmax_scratch_bytes(void) { return logits_argmax_scratch_bytes(); }

@@ -61,6 +61,7 @@ int launch_wait_selftest(int limit_ms, cudaStream_t st);
 void init_enc_attn_attrs();
 void init_dec_linear_attrs();
 void init_logits_argmax_attrs();
+void init_gemm_attrs();
 void init_align_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
@@ -89,6 +90,12 @@ size_t logits_argmax_scratch_bytes();
 int launch_logits_argmax(const void* x, int ldx, const void* emb, int V, int k, int m, const unsigned char* sup,
                          int* tok, int* done, int* ctr, int maxT, int prompt_len, int eos, int bs1, int bs2,
                          void* logits, bool advance, void* scratch, size_t scratch_bytes, cudaStream_t st);
+
+// C = rh(A B^T + bias) on the tensor cores (gemm.cu): A [M][lda], B [N][K] (weights), bias [N] (may be null);
+// mode 0 C [M][ldc]; 1 the same after the exact-erf GELU; 2 head blocks: C[m][n] at c + (n / 64) blk + m 64 + n % 64.
+// N a multiple of 128, K of 64, 16-byte aligned operands and row pitches.
+int launch_gemm_bias(const void* a, int lda, const void* w, const void* bias, void* c, long ldc, int M, int N, int K,
+                     int mode, long blk, cudaStream_t st);
 
 // the DTW cost of the token timestamps for a batch of clips (align.cu)
 int launch_align_cost(const void* align, const int* rows, const int* cols, int n, int np, int mt, int na, void* cost,
