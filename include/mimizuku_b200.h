@@ -110,8 +110,10 @@ int mmz_add_layernorm(void* x, const void* d, const void* w, const void* b, void
  * rounded value first (lin + gelu_inplace, kernels/whisper.cu:107-112); mode 2 stores C[i][j] at
  * c + (j / 64) * blk + i * 64 + j % 64, the decoder's head-contiguous cross k/v layout ([layer][k|v][head][1500][64]
  * with blk = 1500 * 64: model.rs:614-623 and fill_bias_heads, whisper.cu:99-104). n a multiple of 128, k of 64,
- * 16-byte aligned operands and row pitches. Replaces the encoder's cuBLAS GEMMs onto bias images (src/gpu.rs:208-236);
- * the summation order differs from cuBLAS's, so results agree to fp32 rounding before the final fp16 rounding. */
+ * 16-byte aligned operands and row pitches. Where n is a multiple of 256 and m > 128 the tiles are 256 x 256 on pairs of
+ * CTAs (thread-block clusters of two), else 128 x 256 or 128 x 128 on one CTA. Replaces the encoder's cuBLAS GEMMs onto
+ * bias images (src/gpu.rs:208-236); the summation order differs from cuBLAS's, so results agree to fp32 rounding
+ * before the final fp16 rounding. */
 int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void* c, long long ldc, int m, int n, int k,
                   int mode, long long blk, void* stream);
 
@@ -259,6 +261,14 @@ int mmz_engine_lanes(mmz_engine* e);
  * Takes effect at the next encode. */
 int mmz_engine_set_enc_attn(mmz_engine* e, int unfused);
 int mmz_engine_enc_attn(mmz_engine* e);
+/* Encoder GEMMs of an engine on this library's kernels: 0 cuBLASLt for every linear layer (the bias in its epilogue,
+ * GELU as a separate kernel, the cross k/v as strided-batched products onto the head blocks); 1 (the default) this
+ * library's tensor-core GEMM (mmz_gemm_bias) for the qkv projection, fc1 with GELU in its epilogue and the cross k/v
+ * projection stored straight into the [layer][k|v][head][1500][64] blocks, cuBLASLt for the others. The sums associate differently
+ * from cuBLAS's, so the encoder output agrees with the other setting to fp32 rounding. No effect on a fatbin image.
+ * Takes effect at the next encode. */
+int mmz_engine_set_enc_gemm(mmz_engine* e, int mode);
+int mmz_engine_enc_gemm(mmz_engine* e);
 /* Device address of an engine buffer: "tok", "done", "ctr", "align", "logits", "eh", "eqkv", "eatt", "xkv", "mel",
  * "kc", "vc", "x", "hb", "att", "aslot"; NULL if unknown. */
 void* mmz_engine_buffer(mmz_engine* e, const char* name);

@@ -91,6 +91,8 @@ SIGNATURES = {
     "mmz_engine_lanes": (_I, [_P]),
     "mmz_engine_set_enc_attn": (_I, [_P, _I]),
     "mmz_engine_enc_attn": (_I, [_P]),
+    "mmz_engine_set_enc_gemm": (_I, [_P, _I]),
+    "mmz_engine_enc_gemm": (_I, [_P]),
     "mmz_engine_buffer": (_P, [_P, ctypes.c_char_p]),
     "mmz_engine_stream": (_P, [_P]),
     "mmz_engine_sync": (_I, [_P]),

@@ -236,6 +236,8 @@ int mmz_engine_set_lanes(mmz_engine* e, int lanes) { return e ? e->e->set_lanes(
 int mmz_engine_lanes(mmz_engine* e) { return e ? e->e->lanes() : 0; }
 int mmz_engine_set_enc_attn(mmz_engine* e, int unfused) { return e ? e->e->set_enc_attn(unfused) : fail("null engine"); }
 int mmz_engine_enc_attn(mmz_engine* e) { return e ? e->e->enc_attn() : -1; }
+int mmz_engine_set_enc_gemm(mmz_engine* e, int mode) { return e ? e->e->set_enc_gemm(mode) : fail("null engine"); }
+int mmz_engine_enc_gemm(mmz_engine* e) { return e ? e->e->enc_gemm() : -1; }
 void* mmz_engine_buffer(mmz_engine* e, const char* name) { return e && name ? e->e->buffer(name) : nullptr; }
 void* mmz_engine_stream(mmz_engine* e) { return e ? (void*)e->e->stream() : nullptr; }
 int mmz_engine_sync(mmz_engine* e) {

@@ -749,6 +749,7 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     if (gn < 1 || gn > eg_ || slot0 < 0 || slot0 + gn > bmax_) return fail("encode: bad group");
     const int d = dm_.d, nm = dm_.n_mels, nh = dm_.nh, ff = dm_.ff, nl = dm_.dec_layers;
     const long r1 = (long)gn * NFRAMES, r2 = (long)gn * TENC_;
+    const bool tc = enc_tc_ && k_->native();
     if (mel16 != mel_) CUDA_CK(cudaMemcpyAsync(mel_, mel16, (size_t)gn * nm * NFRAMES * 2, cudaMemcpyDeviceToDevice, st_));
     CK(k_->im2col1(mel_, x1_, r1 * 3 * nm, nm, st_));
     CK(lin_enc(x1_, 3 * nm, conv1_, h1_, d, r1, d, 3 * nm));
@@ -760,13 +761,18 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     CK(k_->layernorm(ex_, enc_[0].ln1, eh_, r2, d, st_));
     for (size_t i = 0; i < enc_.size(); i++) {
         const EncLayer& l = enc_[i];
-        CK(lin_enc(eh_, d, l.qkv, eqkv_, 3 * d, r2, 3 * d, d));
+        if (tc) CK(launch_gemm_bias(eh_, d, l.qkv.w, l.qkv.b, eqkv_, 3 * d, r2, 3 * d, d, 0, 0, st_));
+        else CK(lin_enc(eh_, d, l.qkv, eqkv_, 3 * d, r2, 3 * d, d));
         if (enc_unfused_) CK(enc_attn_unfused(gn));
         else CK(k_->enc_attn(eqkv_, eatt_, gn, d, nh, st_));
         CK(lin_enc(eatt_, d, l.o, eh_, d, r2, d, d));
         CK(k_->add_layernorm(ex_, eh_, l.ln2, eh_, r2, d, st_));
-        CK(lin_enc(eh_, d, l.fc1, ef_, ff, r2, ff, d));
-        CK(k_->gelu(ef_, r2 * ff, st_));
+        if (tc) {
+            CK(launch_gemm_bias(eh_, d, l.fc1.w, l.fc1.b, ef_, ff, r2, ff, d, 1, 0, st_));
+        } else {
+            CK(lin_enc(eh_, d, l.fc1, ef_, ff, r2, ff, d));
+            CK(k_->gelu(ef_, r2 * ff, st_));
+        }
         CK(lin_enc(ef_, ff, l.fc2, eh_, d, r2, d, ff));
         const Ln& next = i + 1 < enc_.size() ? enc_[i + 1].ln1 : eln_;
         CK(k_->add_layernorm(ex_, eh_, next, eh_, r2, d, st_));
@@ -777,6 +783,10 @@ int Engine::encode_dev(const void* mel16, int gn, int slot0) {
     for (int c = 0; c < gn; c++) {
         void* dst = (char*)xkv_buf_ + 2 * (size_t)(slot0 + c) * xkv;
         const void* xc = (char*)eh_ + 2 * (size_t)c * TENC_ * d;
+        if (tc) {
+            CK(launch_gemm_bias(xc, d, xkv_.w, xkv_.b, dst, 0, TENC_, nblk * HDIM, d, 2, (long)TENC_ * HDIM, st_));
+            continue;
+        }
         const int r = gemm_bias(xc, d, xkv_.w, (long long)HDIM * d, xkv_.b, dst, HDIM, (long long)TENC_ * HDIM, TENC_,
                                 HDIM, d, nblk);
         if (r == 0) continue;
@@ -808,6 +818,12 @@ int Engine::enc_attn_unfused(int gn) {
         CK(matmul(false, false, HDIM, TENC_, TENC_, 1.f, v, 3 * d, HDIM, esc_, TENC_, (long long)TENC_ * TENC_, 0.f,
                   out, d, HDIM, nh));
     }
+    return 0;
+}
+
+int Engine::set_enc_gemm(int mode) {
+    if (mode != 0 && mode != 1) return fail("set_enc_gemm: 0 (cuBLASLt) or 1 (this library's tensor-core GEMM)");
+    enc_tc_ = mode == 1;
     return 0;
 }
 

@@ -95,6 +95,12 @@ class Engine {
     // (cuBLAS scores into a [heads][1500][1500] buffer, row softmax, cuBLAS P.V; --enc-attn cublas, main.rs:37, 179)
     int set_enc_attn(int unfused);
     int enc_attn() const { return enc_unfused_ ? 1 : 0; }
+    // encoder GEMMs of the native image: 0 cuBLASLt with the bias in its epilogue for every linear layer (GELU as a
+    // separate kernel, the cross k/v as strided-batched products onto the head blocks); 1 (the default) this
+    // library's tensor-core GEMM (mmz_gemm_bias) for qkv, fc1 with its GELU in the epilogue and the cross k/v
+    // projection stored into the head blocks, cuBLASLt for the others (o, fc2, the convolutions: faster there)
+    int set_enc_gemm(int mode);
+    int enc_gemm() const { return enc_tc_ ? 1 : 0; }
 
    private:
     int lin(const void* x, int ldx, const Lin& l, void* y, int ldy, int m, int n, int k);
@@ -130,6 +136,7 @@ class Engine {
     cublasHandle_t blas_ = nullptr;
     int lanes_ = 1;
     bool enc_unfused_ = false;
+    bool enc_tc_ = true;
     void* esc_ = nullptr;  // the unfused encoder attention's scores, allocated on first use
     bool lanes_ok_ = false;          // lanes_rows_match() found the half-batch rows equal
     cudaStream_t st2_ = nullptr;     // second decoder lane

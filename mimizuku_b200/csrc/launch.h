@@ -14,6 +14,7 @@ struct DevCtx {
     unsigned* status = nullptr;            // device address of the status word (4 x u32)
     unsigned long long limit_ns = 1000000000ull;  // bound on every in-kernel wait
     int sms = 0;
+    int gemm_pairs = 0;  // clusters of two gemm_pair_kernel CTAs that fit the device at once (0: none)
 };
 
 // context of the current device, initialised on first use (call mmz_init before any stream capture)
@@ -61,7 +62,7 @@ int launch_wait_selftest(int limit_ms, cudaStream_t st);
 void init_enc_attn_attrs();
 void init_dec_linear_attrs();
 void init_logits_argmax_attrs();
-void init_gemm_attrs();
+void init_gemm_attrs(DevCtx& c);
 void init_align_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set

@@ -72,7 +72,7 @@ static void init_ctx(DevCtx& c, int dev) {
     init_enc_attn_attrs();
     init_dec_linear_attrs();
     init_logits_argmax_attrs();
-    init_gemm_attrs();
+    init_gemm_attrs(c);
     init_align_attrs();
     cudaGetLastError();
     c.ok = true;

@@ -171,6 +171,19 @@ class Engine:
             raise MmzError("enc_attn: 'flash' or 'cublas'")
         _check(lib.mmz_engine_set_enc_attn(self._h, 1 if mode == "cublas" else 0), "set_enc_attn")
 
+    @property
+    def enc_gemm(self):
+        """Encoder GEMMs: "native" (the default: this library's tensor-core GEMM for qkv, fc1 + GELU and the cross
+        k/v projection into the head blocks) or "cublaslt" (every linear layer on cuBLASLt, GELU and the cross k/v
+        layout separate)."""
+        return "native" if lib.mmz_engine_enc_gemm(self._h) == 1 else "cublaslt"
+
+    @enc_gemm.setter
+    def enc_gemm(self, mode):
+        if mode not in ("cublaslt", "native"):
+            raise MmzError("enc_gemm: 'cublaslt' or 'native'")
+        _check(lib.mmz_engine_set_enc_gemm(self._h, 1 if mode == "native" else 0), "set_enc_gemm")
+
     def buffer(self, name):
         p = lib.mmz_engine_buffer(self._h, name.encode())
         if not p:

@@ -11,6 +11,8 @@
     python -m mimizuku_b200.profile_kernels ln             add_layernorm at the encoder's 12000 x 1280
     python -m mimizuku_b200.profile_kernels logmel         the GPU log-mel of 32 synthetic 30 s clips (128 mel bins)
     python -m mimizuku_b200.profile_kernels align          timestamp cost and DTW of 32 clips x 223 tokens x 10 heads
+    python -m mimizuku_b200.profile_kernels gemm [mode]    the encoder's qkv projection (12000 x 3840 x 1280) on the
+                                                           tensor-core GEMM; mode 1: fc1 with GELU (12000 x 5120 x 1280)
 """
 import sys
 
@@ -99,6 +101,15 @@ def main(argv):
         work = torch.empty(m.log_mel_gpu_work_bytes(n), dtype=torch.uint8, device="cuda")
         for _ in range(4):
             m.log_mel_gpu(audio, lens, 128, out, work=work)
+    elif which == "gemm":
+        mode = int(argv[1]) if len(argv) > 1 else 0
+        M, N, K = (12000, 5120, 1280) if mode == 1 else (12000, 3840, 1280)
+        a = torch.randn(M, K, device="cuda", dtype=torch.float16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.float16) * 0.03
+        b = torch.randn(N, device="cuda", dtype=torch.float16)
+        c = torch.empty(M, N, device="cuda", dtype=torch.float16)
+        for _ in range(4):
+            m.gemm_bias(a, w, b, c, mode=mode)
     elif which == "align":
         n, mt, na, np_, rows = 32, 448, 10, 4, 223
         align = torch.rand(n, mt, na, 1500, device="cuda").half()

@@ -1,0 +1,46 @@
+"""The engine's encoder on this library's tensor-core GEMM (qkv, fc1 with GELU in the epilogue, the cross k/v
+projection stored into the head blocks; src/model.rs:551-623) against the same engine on cuBLASLt and against the
+reference-kernel engine: cross k/v within fp16 noise, greedy tokens in lockstep (near-ties only)."""
+import numpy as np
+import pytest
+
+import _oracle as O
+from test_gpu_engine import _clips, _lockstep
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", ["TINY", "LARGE_V3_TURBO"])
+def test_engine_encoder_on_tensor_core_gemm(cuda, ref, name):
+    import mimizuku_b200 as m
+    torch = cuda
+    cfg = getattr(m, name)
+    b = 3 if name == "TINY" else 9
+    mel, frames = _clips(b, cfg.n_mels, seed=7)
+    sup = [cfg.eos]
+    tc = m.Engine(cfg, bmax=b, eg=8, seed=13, suppress=sup)
+    lt = m.Engine(cfg, bmax=b, eg=8, seed=13, suppress=sup)
+    refe = m.Engine(cfg, bmax=b, eg=8, seed=13, suppress=sup, kernel_image=O.REF_FATBIN)
+    tc.enc_gemm = "native"
+    lt.enc_gemm = "cublaslt"
+    assert tc.enc_gemm == "native" and lt.enc_gemm == "cublaslt"
+    mel16 = torch.from_numpy(mel.astype(np.float16)).cuda()
+    for e in (tc, lt, refe):
+        e.encode(mel16[:2].data_ptr(), 2, 0)  # two groups: 2 clips, then the rest
+        e.encode(mel16[2:].data_ptr(), b - 2, 2)
+        e.sync()
+    n = b * cfg.dec_layers * 2 * cfg.d * 1500
+    xkv = {}
+    for key, e in (("tc", tc), ("lt", lt), ("ref", refe)):
+        a = np.empty(n, np.float16)
+        O.d2h(a, e.buffer("xkv"))
+        xkv[key] = a.astype(np.float32)
+    rel = lambda a, r: float(np.sqrt(((a - r) ** 2).sum() / (r ** 2).sum()))  # noqa: E731
+    assert rel(xkv["tc"], xkv["lt"]) < 5e-3, rel(xkv["tc"], xkv["lt"])
+    assert rel(xkv["tc"], xkv["ref"]) < 5e-3, rel(xkv["tc"], xkv["ref"])
+    assert np.abs(xkv["tc"] - xkv["ref"]).max() < 0.06
+    diverged, compared = _lockstep(cfg, tc, refe, b, 24)
+    assert diverged <= max(1, compared // 20), (diverged, compared)
+    assert m.status()[0] == 0
+    for e in (tc, lt, refe):
+        e.close()

@@ -21,20 +21,29 @@ def _close(got, want):
     return bool((err <= tol).all()), float(err.max())
 
 
+@pytest.mark.parametrize("impl", ["pair", "single"])
 @pytest.mark.parametrize("M,N,K,mode", [(12000, 3840, 1280, 0), (12000, 1280, 1280, 0), (3000, 5120, 1280, 1),
                                         (24000, 1280, 384, 1), (12000, 1280, 5120, 0), (100, 256, 64, 0),
-                                        (1500, 10240, 1280, 2), (1500, 2560, 384, 2)])
-def test_gemm_bias(cuda, M, N, K, mode):
+                                        (1500, 10240, 1280, 2), (1500, 2560, 384, 2), (1100, 512, 256, 0),
+                                        (300, 768, 128, 1), (13300, 512, 128, 0), (13300, 512, 128, 2)])
+def test_gemm_bias(cuda, monkeypatch, impl, M, N, K, mode):
+    """Both kernels: pairs of CTAs on 256 x 256 tiles (the default where N is a multiple of 256 and M > 128; the last
+    row tile of 1100 rows leaves the second CTA of its pair wholly past the rows; on 148 SMs the last round of the
+    1280- and 3840-column shapes is cut into 64-column pieces, that of 13300 x 512 into 128-column pieces) and one CTA
+    per 128-row tile."""
     import mimizuku_b200 as m
     torch = cuda
+    if impl == "single":
+        monkeypatch.setenv("MMZ_TEST_GEMM_1SM", "1")
     g = torch.Generator(device="cuda").manual_seed(M + N + K + mode)
     a = torch.randn(M, K, device="cuda", generator=g).half()
     w = (torch.randn(N, K, device="cuda", generator=g) * 0.03).half()
     b = (torch.randn(N, device="cuda", generator=g) * 0.1).half()
     want = _ref(torch, a, w, b, mode)
     if mode == 2:
-        blk = 1500 * 64
-        c = torch.full((N // 64, 1500, 64), 7.0, dtype=torch.float16, device="cuda")
+        rows = max(M, 1500)  # a block holds 1500 rows (the encoder length), more when M is larger
+        blk = rows * 64
+        c = torch.full((N // 64, rows, 64), 7.0, dtype=torch.float16, device="cuda")
         m.gemm_bias(a, w, b, c, mode=2, blk=blk)
         torch.cuda.synchronize()
         got = c[:, :M, :].permute(1, 0, 2).reshape(M, N).float()
