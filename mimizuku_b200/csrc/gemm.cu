@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 //                      both CTAs' `accf` barriers; TMEM is allocated and released by warp 1 of both CTAs
 //   warps 2-9          epilogue in each CTA on its own TMEM rows (as above); the accumulator is released by arrivals
 //                      of both CTAs' epilogue warps on the even CTA's `acce` barrier
-// No copy is multicast: each CTA fetches its own operand halves.
+// Each CTA fetches its own operand halves: no copy lands in both CTAs.
 namespace gp {
 constexpr int BMC = 128;                // rows per CTA (the pair's MMA has M = 256)
 constexpr int BN = 256;                 // tile columns (MMA N)

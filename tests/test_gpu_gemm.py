@@ -25,12 +25,12 @@ def _close(got, want):
 @pytest.mark.parametrize("M,N,K,mode", [(12000, 3840, 1280, 0), (12000, 1280, 1280, 0), (3000, 5120, 1280, 1),
                                         (24000, 1280, 384, 1), (12000, 1280, 5120, 0), (100, 256, 64, 0),
                                         (1500, 10240, 1280, 2), (1500, 2560, 384, 2), (1100, 512, 256, 0),
-                                        (300, 768, 128, 1), (13300, 512, 128, 0), (13300, 512, 128, 2)])
+                                        (300, 768, 128, 1), (13300, 512, 128, 0), (13300, 512, 128, 2),
+                                        (600, 512, 64, 0), (200, 256, 1280, 1)])
 def test_gemm_bias(cuda, monkeypatch, impl, M, N, K, mode):
     """Both kernels: pairs of CTAs on 256 x 256 tiles (the default where N is a multiple of 256 and M > 128; the last
-    row tile of 1100 rows leaves the second CTA of its pair wholly past the rows; on 148 SMs the last round of the
-    1280- and 3840-column shapes is cut into 64-column pieces, that of 13300 x 512 into 128-column pieces) and one CTA
-    per 128-row tile."""
+    row tile of 1100 rows leaves the second CTA of its pair wholly past the rows; K = 64 is one stage per tile; 200
+    rows are one row tile) and one CTA per 128-row tile."""
     import mimizuku_b200 as m
     torch = cuda
     if impl == "single":
