@@ -507,7 +507,7 @@ int launch_self_attn(const void* qkv, void* kc, void* vc, void* out, const int* 
     const uint64_t dims[2] = {(uint64_t)d, (uint64_t)batch * maxT};
     const uint64_t strides[1] = {(uint64_t)d * 2};
     const uint32_t box[2] = {HD, STILE};
-    if (make_tmap_2d(&km, kc, dims, strides, box, true) || make_tmap_2d(&vm, vc, dims, strides, box, false))
+    if (make_tmap_2d(&km, kc, dims, strides, box, 128) || make_tmap_2d(&vm, vc, dims, strides, box, 0))
         return fail("self_attn: cuTensorMapEncodeTiled failed");
     dim3 grid(d / HD, batch);
     return check_pdl(launch_pdl(self_attn_kernel, grid, dim3(128), sizeof(SelfSmem), st, km, vm, (const h16*)qkv,

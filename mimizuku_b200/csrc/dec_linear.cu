@@ -189,7 +189,7 @@ int launch_dec_linear(const void* x, int ldx, const void* w, const void* bias, v
     const uint32_t wb[2] = {BK, BN};
     const uint64_t xd[2] = {(uint64_t)k, (uint64_t)m}, xs[1] = {(uint64_t)ldx * 2};
     const uint32_t xb[2] = {BK, BM};
-    if (make_tmap_2d(&wm, w, wd, ws, wb, true) || make_tmap_2d(&xm, x, xd, xs, xb, true))
+    if (make_tmap_2d(&wm, w, wd, ws, wb, 128) || make_tmap_2d(&xm, x, xd, xs, xb, 128))
         return fail("dec_linear: cuTensorMapEncodeTiled failed");
     // split K over a cluster of S CTAs (a power of two up to 16, at least one chunk each) so that the launch has up to
     // two CTAs per SM: at m <= 32 the product is a stream over W, and more CTAs keep more of it in flight

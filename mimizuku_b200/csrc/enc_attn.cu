@@ -340,7 +340,7 @@ int launch_enc_flash(const void* qkv, void* out, int groups, int d, cudaStream_t
     const uint64_t dims[3] = {(uint64_t)3 * d, (uint64_t)TENC, (uint64_t)groups};
     const uint64_t strides[2] = {(uint64_t)3 * d * 2, (uint64_t)TENC * 3 * d * 2};
     const uint32_t box[3] = {HD, BM, 1};
-    if (make_tmap_3d(&map, qkv, dims, strides, box, true)) return fail("enc_flash: cuTensorMapEncodeTiled failed");
+    if (make_tmap_3d(&map, qkv, dims, strides, box, 128)) return fail("enc_flash: cuTensorMapEncodeTiled failed");
     dim3 grid(NQT, d / HD, groups);
     return check_pdl(launch_pdl(enc_flash_kernel, grid, dim3(NTHREADS), sizeof(Smem), st, map, (h16*)out, d, dc.status,
                                 dc.limit_ns),

@@ -475,7 +475,7 @@ int launch_gemm_bias(const void* a, int lda, const void* w, const void* bias, vo
     const uint32_t ab[2] = {BK, BM};
     const uint64_t bd[2] = {(uint64_t)K, (uint64_t)N}, bs[1] = {(uint64_t)K * 2};
     const uint32_t bb[2] = {BK, (uint32_t)bn};
-    if (make_tmap_2d(&am, a, ad, as, ab, true) || make_tmap_2d(&bm, w, bd, bs, bb, true))
+    if (make_tmap_2d(&am, a, ad, as, ab, 128) || make_tmap_2d(&bm, w, bd, bs, bb, 128))
         return fail("gemm_bias: cuTensorMapEncodeTiled failed");
     // pairs of CTAs on 256 x 256 tiles where the shape has them (MMZ_TEST_GEMM_1SM=1 keeps one CTA per tile, a test
     // hook); each pair's CTAs load 128-row halves of the weight tile
@@ -483,15 +483,15 @@ int launch_gemm_bias(const void* a, int lda, const void* w, const void* bias, vo
     if (dc.gemm_pairs > 0 && N % 256 == 0 && M > BM && !(one && one[0] == '1')) {
         CUtensorMap cm;
         const uint32_t hb1[2] = {BK, 128};
-        int e = make_tmap_2d(&bm, w, bd, bs, hb1, true);
+        int e = make_tmap_2d(&bm, w, bd, bs, hb1, 128);
         if (mode == 2) {  // [N / 64 blocks][M rows][64]
             const uint64_t cd[3] = {64, (uint64_t)M, (uint64_t)(N / 64)}, cs[2] = {128, (uint64_t)blk * 2};
             const uint32_t cb[3] = {64, 32, 1};
-            e = e || make_tmap_3d(&cm, c, cd, cs, cb, true);
+            e = e || make_tmap_3d(&cm, c, cd, cs, cb, 128);
         } else {
             const uint64_t cd[2] = {(uint64_t)N, (uint64_t)M}, cs[1] = {(uint64_t)ldc * 2};
             const uint32_t cb[2] = {64, 32};
-            e = e || make_tmap_2d(&cm, c, cd, cs, cb, true);
+            e = e || make_tmap_2d(&cm, c, cd, cs, cb, 128);
         }
         if (e) return fail("gemm_bias: cuTensorMapEncodeTiled failed");
         const long T2 = ((M + 255) / 256) * (long)(N / 256);

@@ -31,10 +31,11 @@ const char* last_error();
 // cudaGetLastError after a launch: 0 or fail
 int check_launch(const char* what);
 
+// fp16 tensor maps; swizzle: 0 (none), 64 or 128 (bytes)
 int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], const uint64_t strides[1],
-                 const uint32_t box[2], bool swizzle128);
+                 const uint32_t box[2], int swizzle);
 int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
-                 const uint32_t box[3], bool swizzle128);
+                 const uint32_t box[3], int swizzle);
 
 // Launches `kernel` as a programmatic dependent of the previous kernel in the stream, so that its launch overlaps that
 // kernel's tail; the kernel runs griddep_wait() before it touches memory.

@@ -284,7 +284,7 @@ int launch_logits_argmax(const void* x, int ldx, const void* emb, int V, int k, 
     const uint32_t wb[2] = {BK, BN};
     const uint64_t xd[2] = {(uint64_t)k, (uint64_t)m}, xs[1] = {(uint64_t)ldx * 2};
     const uint32_t xb[2] = {BK, BM};
-    if (make_tmap_2d(&wm, emb, wd, ws, wb, true) || make_tmap_2d(&xm, x, xd, xs, xb, true))
+    if (make_tmap_2d(&wm, emb, wd, ws, wb, 128) || make_tmap_2d(&xm, x, xd, xs, xb, 128))
         return fail("logits_argmax: cuTensorMapEncodeTiled failed");
     const int tiles = (V + BN - 1) / BN;
     const int grid = tiles < dc.sms ? tiles : dc.sms;

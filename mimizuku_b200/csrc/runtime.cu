@@ -127,13 +127,15 @@ static EncodeTiledFn encode_fn() {
 }
 
 static int make_tmap(CUtensorMap* map, int rank, const void* base, const uint64_t* dims, const uint64_t* strides,
-                     const uint32_t* box, bool swizzle128) {
+                     const uint32_t* box, int swizzle) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return -1;
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), (const cuuint64_t*)dims,
                     (const cuuint64_t*)strides, (const cuuint32_t*)box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    swizzle == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                    : swizzle == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                    : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : -1;
 }
@@ -163,13 +165,13 @@ int launch_wait_selftest(int limit_ms, cudaStream_t st) {
 }
 
 int make_tmap_2d(CUtensorMap* map, const void* base, const uint64_t dims[2], const uint64_t strides[1],
-                 const uint32_t box[2], bool swizzle128) {
-    return make_tmap(map, 2, base, dims, strides, box, swizzle128);
+                 const uint32_t box[2], int swizzle) {
+    return make_tmap(map, 2, base, dims, strides, box, swizzle);
 }
 
 int make_tmap_3d(CUtensorMap* map, const void* base, const uint64_t dims[3], const uint64_t strides[2],
-                 const uint32_t box[3], bool swizzle128) {
-    return make_tmap(map, 3, base, dims, strides, box, swizzle128);
+                 const uint32_t box[3], int swizzle) {
+    return make_tmap(map, 3, base, dims, strides, box, swizzle);
 }
 
 }  // namespace mmz
