@@ -11,6 +11,8 @@
     python -m mimizuku_b200.profile_kernels ln             add_layernorm at the encoder's 12000 x 1280
     python -m mimizuku_b200.profile_kernels logmel         the GPU log-mel of 32 synthetic 30 s clips (128 mel bins)
     python -m mimizuku_b200.profile_kernels align          timestamp cost and DTW of 32 clips x 223 tokens x 10 heads
+    python -m mimizuku_b200.profile_kernels encode         one encoder group of the large-v3 engine (8 clips), inside the
+                                                           NVTX range "encode" (after one untimed group)
     python -m mimizuku_b200.profile_kernels gemm [mode]    the encoder's qkv projection (12000 x 3840 x 1280) on the
                                                            tensor-core GEMM; mode 1: fc1 with GELU (12000 x 5120 x 1280)
 """
@@ -71,6 +73,17 @@ def main(argv):
         torch.cuda.nvtx.range_push("steps")
         for _ in range(n):
             e.replay()
+        e.sync()
+        torch.cuda.nvtx.range_pop()
+        e.close()
+    elif which == "encode":
+        cfg = m.LARGE_V3
+        e = m.Engine(cfg, bmax=8, eg=8, device=0, seed=1234, suppress=[cfg.eos])
+        mel16 = torch.randn(8, cfg.n_mels, 3000, device="cuda").half()
+        e.encode(mel16.data_ptr(), 8, 0)
+        e.sync()
+        torch.cuda.nvtx.range_push("encode")
+        e.encode(mel16.data_ptr(), 8, 0)
         e.sync()
         torch.cuda.nvtx.range_pop()
         e.close()
