@@ -123,6 +123,15 @@ int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void*
  * differ from the reference kernel's in the last fp16 bit. */
 int mmz_softmax_rows(void* s, long rows, int n, void* stream);
 
+/* The encoder front end's data movement, with the reference kernels' arguments (kernels/whisper.cu:115-139, launched
+ * at src/model.rs:553-559): im2col1 writes conv1's operand X[g][t][ci * 3 + k] = mel[g][ci][t + k - 1] (zero outside
+ * the 3000 frames) for the n = groups x 3000 x 3 nm values; im2col2 writes conv2's X[g][t][ci * 3 + k] =
+ * h1[g][2t + k - 1][ci] for the n = groups x 1500 x 3d values; add_pos adds pos[r % period] to each of the `rows` rows
+ * of x [rows][n] in place (f32 sum, one rounding). The same values as the reference kernels', bit for bit. */
+int mmz_im2col1(const void* mel, void* X, long long n, int nm, void* stream);
+int mmz_im2col2(const void* h1, void* X, long long n, int d, void* stream);
+int mmz_add_pos(void* x, const void* pos, long long rows, int n, int period, void* stream);
+
 /* Decoder linear layer at m <= 32 sequences: y[m][n] = rh(x[m][:k] . w[n][:k] + bias[n]) (fp16 in and out, fp32
  * accumulation; bias may be NULL), then GELU when gelu != 0 (fc1 followed by gelu_inplace, kernels/whisper.cu:107-112). x [m][ldx],
  * w [n][k], y [m][ldy]; k a multiple of 64, x and w 16-byte aligned. Replaces the decoder step's cuBLAS GEMMs onto

@@ -67,6 +67,9 @@ SIGNATURES = {
     "mmz_dtw_times": (_I, [_P, _P, _P, _I, _I, _P, _P]),
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "mmz_softmax_rows": (_I, [_P, _L, _I, _P]),
+    "mmz_im2col1": (_I, [_P, _P, _LL, _I, _P]),
+    "mmz_im2col2": (_I, [_P, _P, _LL, _I, _P]),
+    "mmz_add_pos": (_I, [_P, _P, _LL, _I, _I, _P]),
     "mmz_gemm_bias": (_I, [_P, _I, _P, _P, _P, _LL, _I, _I, _I, _I, _LL, _P]),
     "mmz_logits_argmax_scratch_bytes": (_ULL, []),
     "mmz_logits_argmax": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P, _ULL, _P]),
@@ -267,6 +270,23 @@ def softmax_rows(s, n=None, rows=None, stream=None):
     n = n if n is not None else s.shape[-1]
     rows = rows if rows is not None else s.numel() // n
     _check(lib.mmz_softmax_rows(_ptr(s), rows, n, _stream(stream)), "softmax_rows")
+
+
+def im2col1(mel, X, nm, n=None, stream=None):
+    """conv1's operand from the log-mel: X [groups][3000][3 nm] from mel [groups][nm][3000] (fp16 device tensors)."""
+    _check(lib.mmz_im2col1(_ptr(mel), _ptr(X), n if n is not None else X.numel(), nm, _stream(stream)), "im2col1")
+
+
+def im2col2(h1, X, d, n=None, stream=None):
+    """conv2's operand: X [groups][1500][3d] from conv1's output h1 [groups][3000][d] (fp16 device tensors)."""
+    _check(lib.mmz_im2col2(_ptr(h1), _ptr(X), n if n is not None else X.numel(), d, _stream(stream)), "im2col2")
+
+
+def add_pos(x, pos, period, n=None, rows=None, stream=None):
+    """x[r] += pos[r % period] in place, x [rows][n] and pos [period][n] fp16 device tensors."""
+    n = n if n is not None else x.shape[-1]
+    rows = rows if rows is not None else x.numel() // n
+    _check(lib.mmz_add_pos(_ptr(x), _ptr(pos), rows, n, period, _stream(stream)), "add_pos")
 
 
 def logits_argmax_scratch_bytes():

@@ -108,6 +108,19 @@ int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void*
 
 int mmz_softmax_rows(void* s, long rows, int n, void* stream) { return launch_softmax_rows(s, rows, n, S(stream)); }
 
+int mmz_im2col1(const void* mel, void* X, long long n, int nm, void* stream) {
+    if (n < 0 || nm < 1) return fail("im2col1: bad shape");
+    return launch_im2col1(mel, X, (long)n, nm, S(stream));
+}
+int mmz_im2col2(const void* h1, void* X, long long n, int d, void* stream) {
+    if (n < 0 || d < 1) return fail("im2col2: bad shape");
+    return launch_im2col2(h1, X, (long)n, d, S(stream));
+}
+int mmz_add_pos(void* x, const void* pos, long long rows, int n, int period, void* stream) {
+    if (rows < 0 || n < 1 || period < 1) return fail("add_pos: bad shape");
+    return launch_add_pos(x, pos, (long)rows, n, period, S(stream));
+}
+
 unsigned long long mmz_logits_argmax_scratch_bytes(void) { return logits_argmax_scratch_bytes(); }
 
 int mmz_logits_argmax(const void* x, int ldx, const void* emb, int vocab, int d, int m, const unsigned char* sup,

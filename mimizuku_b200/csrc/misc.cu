@@ -121,6 +121,65 @@ __global__ void im2col2_kernel(const h16* __restrict__ h1, h16* __restrict__ X, 
     X[i] = (tt >= 0 && tt < NFR) ? h1[((long)g * NFR + tt) * d + ci] : h(0.f);
 }
 
+// The same two operands with wide accesses (the engine's path; the kernels above serve shapes these do not take):
+//   im2col1_tile_kernel  a CTA takes 64 frames of one clip, stages mel[g][all channels][t0 - 1 .. t0 + 64] in shared
+//                        memory (the transpose: channel-major in, frame-major out) and writes its 64 rows of 3 nm
+//                        values with 16-byte stores; 3 nm a multiple of 8
+//   im2col2_vec_kernel   a thread takes 8 channels of one output row: three 16-byte loads (input rows 2t - 1, 2t,
+//                        2t + 1) and three 16-byte stores of the 24 interleaved values; d a multiple of 8
+constexpr int I1T = 64;  // frames per CTA of im2col1_tile_kernel
+
+// grid (ceil(NFR / 64), clips), block 256, dynamic shared memory nm x 66 halves
+__global__ void __launch_bounds__(256) im2col1_tile_kernel(const h16* __restrict__ mel, h16* __restrict__ X, int nm) {
+    extern __shared__ h16 tile[];  // [channel][I1T + 2]: frames t0 - 1 .. t0 + I1T
+    constexpr int W = I1T + 2;
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    const int g = blockIdx.y, t0 = blockIdx.x * I1T;
+    for (int i = threadIdx.x; i < nm * W; i += blockDim.x) {
+        const int ci = i / W, tt = t0 - 1 + i % W;
+        tile[i] = (tt >= 0 && tt < NFR) ? mel[((long)g * nm + ci) * NFR + tt] : h(0.f);
+    }
+    __syncthreads();
+    const int cpr = 3 * nm / 8;  // 16-byte chunks per output row
+    for (int i = threadIdx.x; i < I1T * cpr; i += blockDim.x) {
+        const int tr = i / cpr, c = i % cpr, t = t0 + tr;
+        if (t >= NFR) break;  // i grows with tr: every later i is past the clip too
+        __align__(16) h16 v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int j = c * 8 + e;  // X column: channel j / 3, tap j % 3
+            v[e] = tile[(j / 3) * W + tr + j % 3];
+        }
+        *reinterpret_cast<uint4*>(X + ((long)g * NFR + t) * 3 * nm + c * 8) = *reinterpret_cast<const uint4*>(v);
+    }
+}
+
+__global__ void im2col2_vec_kernel(const h16* __restrict__ h1, h16* __restrict__ X, long rows, int d) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    const int c8 = d / 8;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * c8) return;
+    const long r = i / c8;
+    const int c = (int)(i % c8), t = (int)(r % TENC);
+    const long g = r / TENC;
+    uint4 in[3];
+#pragma unroll
+    for (int k = 0; k < 3; k++) {
+        const int tt = 2 * t + k - 1;
+        in[k] = (tt >= 0 && tt < NFR) ? *reinterpret_cast<const uint4*>(h1 + (g * NFR + tt) * d + c * 8)
+                                      : make_uint4(0, 0, 0, 0);
+    }
+    const h16* a = reinterpret_cast<const h16*>(in);
+    __align__(16) h16 o[24];
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+#pragma unroll
+        for (int k = 0; k < 3; k++) o[e * 3 + k] = a[k * 8 + e];
+    uint4* dst = reinterpret_cast<uint4*>(X + r * 3 * d + c * 24);
+#pragma unroll
+    for (int u = 0; u < 3; u++) dst[u] = reinterpret_cast<const uint4*>(o)[u];
+}
+
 // exact (erf) GELU over half2 pairs (kernels/whisper.cu:106-113)
 __device__ __forceinline__ float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 __global__ void gelu_kernel(__half2* x, long n2) {
@@ -146,6 +205,27 @@ __global__ void gelu8_kernel(uint4* x, long n8) {
 }
 
 // x[r, c] += pos[r % period, c] (kernels/whisper.cu:115-119)
+// the same, 8 values per thread with 16-byte accesses (n a multiple of 8): each sum in f32, rounded once, as above
+__global__ void add_pos_vec_kernel(h16* x, const h16* __restrict__ pos, long rows, int n, int period) {
+    griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    const int n8 = n / 8;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * n8) return;
+    const long r = i / n8;
+    const int c = (int)(i % n8);
+    uint4* px = reinterpret_cast<uint4*>(x + r * n + c * 8);
+    uint4 xv = *px;
+    const uint4 pv = *reinterpret_cast<const uint4*>(pos + (r % period) * n + c * 8);
+    __half2* xh = reinterpret_cast<__half2*>(&xv);
+    const __half2* ph = reinterpret_cast<const __half2*>(&pv);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const float2 a = __half22float2(xh[e]), b = __half22float2(ph[e]);
+        xh[e] = __float22half2_rn(make_float2(a.x + b.x, a.y + b.y));
+    }
+    *px = xv;
+}
+
 __global__ void add_pos_kernel(h16* x, const h16* __restrict__ pos, long rows, int n, int period) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -284,12 +364,21 @@ int launch_advance(int* ctr, cudaStream_t st) {
 }
 
 int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st) {
+    const long row = 3L * nm * NFR;  // one clip's operand
+    if (nm > 0 && (3 * nm) % 8 == 0 && n % row == 0 && ((uintptr_t)X & 15) == 0 && nm * (I1T + 2) * 2 <= 48 * 1024)
+        return check_pdl(launch_pdl(im2col1_tile_kernel, dim3((NFR + I1T - 1) / I1T, (unsigned)(n / row)), dim3(256),
+                                    (size_t)nm * (I1T + 2) * 2, st, (const h16*)mel, (h16*)X, nm),
+                         "im2col1");
     return check_pdl(launch_pdl(im2col1_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (const h16*)mel, (h16*)X, n,
                                 nm),
                      "im2col1");
 }
 
 int launch_im2col2(const void* h1, void* X, long n, int d, cudaStream_t st) {
+    if (d > 0 && d % 8 == 0 && n % (3L * d) == 0 && ((uintptr_t)h1 & 15) == 0 && ((uintptr_t)X & 15) == 0)
+        return check_pdl(launch_pdl(im2col2_vec_kernel, dim3(blocks(n / 3 / 8, 256)), dim3(256), 0, st,
+                                    (const h16*)h1, (h16*)X, n / (3L * d), d),
+                         "im2col2");
     return check_pdl(launch_pdl(im2col2_kernel, dim3(blocks(n, 256)), dim3(256), 0, st, (const h16*)h1, (h16*)X, n, d),
                      "im2col2");
 }
@@ -303,6 +392,10 @@ int launch_gelu(void* x, long n, cudaStream_t st) {
 }
 
 int launch_add_pos(void* x, const void* pos, long rows, int n, int period, cudaStream_t st) {
+    if (n % 8 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)pos & 15) == 0)
+        return check_pdl(launch_pdl(add_pos_vec_kernel, dim3(blocks(rows * (n / 8), 256)), dim3(256), 0, st, (h16*)x,
+                                    (const h16*)pos, rows, n, period),
+                         "add_pos");
     return check_pdl(launch_pdl(add_pos_kernel, dim3(blocks(rows * n, 256)), dim3(256), 0, st, (h16*)x, (const h16*)pos,
                                 rows, n, period),
                      "add_pos");
