@@ -53,6 +53,17 @@ def test_kernel_entry_points_validate_shapes_before_touching_a_device():
     assert m.lib.mmz_cross_attn_scratch_bytes(32, 1280) == 32 * 20 * (1500 * 4 + 24 * 8 + 24 * 64 * 4)
     assert m.lib.mmz_self_attn(None, None, None, None, None, None, 1, 600, 384, None) != 0
     assert m.lib.mmz_layernorm(None, None, None, None, 1, 4097, 1e-5, None) != 0
+    # the tensor-core GEMM: n a multiple of 128, k of 64, mode 0-2, 16-byte aligned operands and pitches
+    g = m.lib.mmz_gemm_bias
+    assert g(None, 64, None, None, None, 256, 16, 100, 64, 0, 0, None) != 0  # n
+    assert b"gemm_bias" in m.lib.mmz_last_error()
+    assert g(None, 64, None, None, None, 256, 16, 256, 70, 0, 0, None) != 0  # k
+    assert g(None, 64, None, None, None, 256, 16, 256, 64, 3, 0, None) != 0  # mode
+    assert g(8, 64, 16, None, 16, 256, 16, 256, 64, 0, 0, None) != 0  # a not 16-byte aligned
+    assert g(16, 36, 16, None, 16, 256, 16, 256, 64, 0, 0, None) != 0  # lda below k
+    assert g(16, 64, 16, None, 16, 256, 16, 256, 64, 2, 100, None) != 0  # head blocks smaller than m x 64
+    assert m.lib.mmz_im2col1(None, None, 10, 0, None) != 0
+    assert m.lib.mmz_add_pos(None, None, 4, 8, 0, None) != 0
 
 
 def test_missing_device_is_an_error_not_a_crash():
