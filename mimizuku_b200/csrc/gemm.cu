@@ -210,8 +210,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // M256 N256 K16 MMA stream: CTA r of the pair loads its 128 rows of A and its 128 rows of the weight tile (half of
 // B), and the even CTA issues the MMAs, which read both CTAs' shared memory and leave each CTA its 128 rows x 256
 // columns of the accumulator in its own TMEM. Per SM, 32 KB of operands per 64-wide K step feed 4 x 1 MFLOP of MMA
-// (48 KB in the single-CTA kernel above, which the L2 could not deliver at the tensor cores' rate: 1134 against 1314
-// TFLOP/s on the encoder's qkv projection). The epilogue stages each 32 x 64 output box in shared memory (128-byte
+// (48 KB in the single-CTA kernel above, which ran the encoder's qkv projection at 1134 TFLOP/s against this kernel's
+// 1314). The epilogue stages each 32 x 64 output box in shared memory (128-byte
 // swizzle) and stores it with TMA: with thread-per-row 16-byte stores instead (as in the single-CTA kernel) this
 // kernel took 54.5 against 32.4 us on the 24000 x 1280 x 384 convolution, where the epilogue is the larger part.
 //   warp 0 (each CTA)  TMA producer for its own halves; every copy counts its bytes on the even CTA's `full` barrier,
