@@ -17,6 +17,9 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libmimizuku_b200.so")
+# layernorm, add_layernorm and kv_write under the reference's names and argument lists, for a host that launches
+# kernels by name (built by build.py next to the library)
+DROPIN_FATBIN = os.path.join(_HERE, "dropin_sm100a.fatbin")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is missing; build it with `python mimizuku_b200/build.py`")

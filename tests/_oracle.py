@@ -201,10 +201,11 @@ def normal16(rng, shape, scale=1.0):
 # ------------------------------------------------------------------ the reference's kernels through the driver
 
 class RefKernels:
-    """Loads oracle/_ref/whisper_ref.fatbin (the reference's kernels/whisper.cu, compute_80) into the current CUDA
-    context and launches its kernels by name with explicit argument types, as the reference's gpu.rs does."""
+    """Loads oracle/_ref/whisper_ref.fatbin (the reference's kernels/whisper.cu, compute_80), or another image with
+    the same names, into the current CUDA context and launches its kernels by name with explicit argument types, as the
+    reference's gpu.rs does."""
 
-    def __init__(self):
+    def __init__(self, path=None):
         import torch  # noqa: F401  (creates and binds the primary context)
         torch.cuda.init()
         torch.zeros(1, device="cuda")
@@ -213,7 +214,7 @@ class RefKernels:
         self.cu.cuModuleGetFunction.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_char_p]
         self.cu.cuLaunchKernel.argtypes = [ctypes.c_void_p] + [ctypes.c_uint] * 7 + [
             ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
-        with open(REF_FATBIN, "rb") as f:
+        with open(path or REF_FATBIN, "rb") as f:
             self._image = ctypes.create_string_buffer(f.read())
         self.mod = ctypes.c_void_p()
         rc = self.cu.cuModuleLoadData(ctypes.byref(self.mod), self._image)
