@@ -123,6 +123,13 @@ int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void*
  * differ from the reference kernel's in the last fp16 bit. */
 int mmz_softmax_rows(void* s, long rows, int n, void* stream);
 
+/* Decoder linear layer at 1 <= m <= 8 sequences: y[m][n] = rh(x[m][:k] . w[n][:k] + bias[n]) (bias may be NULL),
+ * equal bit for bit to the reference's gemv kernels (kernels/whisper.cu:501-567), which its host uses instead of
+ * cuBLAS up to 8 rows (src/gpu.rs:211-228): the same per-lane sums and lane butterfly, the weights streamed before the
+ * wait for the kernel before. k a multiple of 8, x and w 16-byte aligned, ldx a multiple of 8. */
+int mmz_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+             void* stream);
+
 /* The encoder front end's data movement, with the reference kernels' arguments (kernels/whisper.cu:115-139, launched
  * at src/model.rs:553-559): im2col1 writes conv1's operand X[g][t][ci * 3 + k] = mel[g][ci][t + k - 1] (zero outside
  * the 3000 frames) for the n = groups x 3000 x 3 nm values; im2col2 writes conv2's X[g][t][ci * 3 + k] =

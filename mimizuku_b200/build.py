@@ -24,9 +24,9 @@ NVCC_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-
                      "--expt-relaxed-constexpr"]
 CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-Wall", "-Wno-unused-function", f"-I{CUDA}/include"]
 
-CU = ["runtime.cu", "dec_attn.cu", "enc_attn.cu", "ln.cu", "misc.cu", "cross_noalloc.cu", "align.cu", "dec_linear.cu", "logmel.cu", "logits_argmax.cu", "gemm.cu"]
+CU = ["runtime.cu", "dec_attn.cu", "enc_attn.cu", "ln.cu", "misc.cu", "cross_noalloc.cu", "align.cu", "dec_linear.cu", "logmel.cu", "logits_argmax.cu", "gemm.cu", "gemv.cu"]
 CPP = ["host_cpu.cpp", "engine.cpp", "capi.cpp"]
-HEADERS = ["common.cuh", "launch.h", "engine.h", "host_cpu.h", "ln_row.cuh"]
+HEADERS = ["common.cuh", "launch.h", "engine.h", "host_cpu.h", "ln_row.cuh", "gemv_row.cuh"]
 # kernels under the reference's own names, as an image its host loads by name (not linked into the library)
 DROPIN_SRC = os.path.join(CSRC, "dropin.cu")
 DROPIN = os.path.join(HERE, "dropin_sm100a.fatbin")

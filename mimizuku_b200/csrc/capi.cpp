@@ -108,6 +108,10 @@ int mmz_gemm_bias(const void* a, int lda, const void* w, const void* bias, void*
 
 int mmz_softmax_rows(void* s, long rows, int n, void* stream) { return launch_softmax_rows(s, rows, n, S(stream)); }
 
+int mmz_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+             void* stream) {
+    return launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, S(stream));
+}
 int mmz_im2col1(const void* mel, void* X, long long n, int nm, void* stream) {
     if (n < 0 || nm < 1) return fail("im2col1: bad shape");
     return launch_im2col1(mel, X, (long)n, nm, S(stream));

@@ -5,9 +5,12 @@
 //                             (x read once, the reference's reduction tree), bit-identical to kernels/whisper.cu:66-82
 //   kv_write                  grid (B), block 256 (model.rs:665): 16-byte copies of the current position's k and v
 //                             into the caches (kernels/whisper.cu:310-317)
+//   gemv_1, _2, _4, _8        grid ceil(N / 32), block 256 (gpu.rs:211-228; the shared memory it passes goes unused):
+//                             gemv_row.cuh, bit-identical to kernels/whisper.cu:501-567
 // The attention kernels need launch settings Gpu::k cannot express (a tensor map, 100+ KB of shared memory, other
 // grids) and stay behind the C-ABI entry points.
 #include "common.cuh"
+#include "gemv_row.cuh"
 #include "ln_row.cuh"
 
 using namespace mmz;
@@ -65,3 +68,14 @@ extern "C" __global__ void kv_write(const h16* qkv, h16* kc, h16* vc, const int*
         }
     }
 }
+
+#define MMZ_GEMV(MR)                                                                                                 \
+    extern "C" __global__ void __launch_bounds__(256) gemv_##MR(const h16* x, int ldx, const h16* W, h16* y, int ldy, \
+                                                                int M, int N, int K, const h16* bias) {               \
+        gemv_rows<MR>(x, ldx, W, y, ldy, M, N, K, bias);                                                             \
+    }
+MMZ_GEMV(1)
+MMZ_GEMV(2)
+MMZ_GEMV(4)
+MMZ_GEMV(8)
+#undef MMZ_GEMV

@@ -128,21 +128,25 @@ class NativeKernels : public Kernels {
     int fill_bias_heads(void* y, const void* bias, long n8, cudaStream_t st) override {
         return ++launches, launch_fill_bias_heads(y, bias, n8, st);
     }
-    int gemv(const void*, int, const void*, void*, int, int, int, int, const void*, cudaStream_t) override { return -2; }
-    // split-K tensor-core product streaming the 133 MB embedding (m <= 32)
+    int gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+             cudaStream_t st) override {
+        return ++launches, launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, st);
+    }
+    // split-K tensor-core product streaming the 133 MB embedding (8 < m <= 32; up to 8 sequences the reference's host
+    // takes its gemv kernels, gpu.rs:211-228, and so does this engine, for the same logits bit for bit)
     int logits(const void* hb, int d, const void* emb, void* out, int vocab, int b, int, cudaStream_t st) override {
-        if (b > 32) return -2;
+        if (b <= 8 || b > 32) return -2;
         return ++launches, launch_dec_linear(hb, d, emb, nullptr, out, vocab, b, vocab, d, false, st);
     }
     // the logits streamed once and reduced to each sequence's token on the GPU, no [b][vocab] logits in memory
-    // (m <= 32, d <= 1280); lgscratch: its zero-initialised scratch, owned by the engine
+    // (8 < m <= 32, d <= 1280); lgscratch: its zero-initialised scratch, owned by the engine
     void* lgscratch = nullptr;
     size_t lgscratch_bytes = 0;
     bool fused_logits = true;
     int logits_argmax(const void* hb, int d, const void* emb, int vocab, int b, const unsigned char* sup, int* tok,
                       int* done, int* ctr, int maxT, int prompt_len, int eos, int bs1, int bs2,
                       cudaStream_t st) override {
-        if (!fused_logits || b > 32 || d > 1280 || !lgscratch) return -2;
+        if (!fused_logits || b <= 8 || b > 32 || d > 1280 || !lgscratch) return -2;
         return ++launches, launch_logits_argmax(hb, d, emb, vocab, d, b, sup, tok, done, ctr, maxT, prompt_len, eos,
                                                 bs1, bs2, nullptr, true, lgscratch, lgscratch_bytes, st);
     }

@@ -62,6 +62,13 @@ def test_kernel_entry_points_validate_shapes_before_touching_a_device():
     assert g(8, 64, 16, None, 16, 256, 16, 256, 64, 0, 0, None) != 0  # a not 16-byte aligned
     assert g(16, 36, 16, None, 16, 256, 16, 256, 64, 0, 0, None) != 0  # lda below k
     assert g(16, 64, 16, None, 16, 256, 16, 256, 64, 2, 100, None) != 0  # head blocks smaller than m x 64
+    # the gemv: 1 <= m <= 8, k a multiple of 8, ldx >= k, ldy >= n
+    v = m.lib.mmz_gemv
+    assert v(None, 16, None, None, 16, 9, 16, 16, None, None) != 0 and b"gemv" in m.lib.mmz_last_error()
+    assert v(None, 16, None, None, 16, 0, 16, 16, None, None) != 0
+    assert v(None, 16, None, None, 16, 1, 16, 12, None, None) != 0
+    assert v(None, 8, None, None, 16, 1, 16, 16, None, None) != 0
+    assert v(8, 16, 16, None, 16, 1, 16, 16, None, None) != 0  # x not 16-byte aligned
     assert m.lib.mmz_im2col1(None, None, 10, 0, None) != 0
     assert m.lib.mmz_add_pos(None, None, 4, 8, 0, None) != 0
 
