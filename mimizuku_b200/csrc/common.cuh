@@ -17,7 +17,7 @@ constexpr int NFR = 3000;   // mel frames (30 s)
 
 // ---- status word: [0] error code (first one wins), [1] kernel id, [2] detail
 enum : unsigned { ST_OK = 0, ST_TIMEOUT = 1, ST_MISALIGNED = 2, ST_BAD_ARG = 3 };
-enum : unsigned { K_ENC = 1, K_SELF = 2, K_CROSS = 3, K_LN = 4, K_LIN = 5, K_SELFTEST = 6, K_LOGITS = 7, K_GEMM = 8 };
+enum : unsigned { K_ENC = 1, K_SELF = 2, K_CROSS = 3, K_LN = 4, K_LIN = 5, K_SELFTEST = 6, K_LOGITS = 7, K_GEMM = 8, K_GEMV = 9 };
 
 __device__ __forceinline__ void report(unsigned* status, unsigned code, unsigned kernel, unsigned detail) {
     if (status && atomicCAS(status, 0u, code) == 0u) {

@@ -58,6 +58,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 int check_pdl(cudaError_t e, const char* what);
 
 void init_dec_attn_attrs(DevCtx& c);
+void init_gemv_attrs();
 // a kernel whose bounded wait runs out on purpose (runtime.cu)
 int launch_wait_selftest(int limit_ms, cudaStream_t st);
 void init_enc_attn_attrs();

@@ -73,6 +73,7 @@ static void init_ctx(DevCtx& c, int dev) {
     init_dec_linear_attrs();
     init_logits_argmax_attrs();
     init_gemm_attrs(c);
+    init_gemv_attrs();
     init_align_attrs();
     cudaGetLastError();
     c.ok = true;

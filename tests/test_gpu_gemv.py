@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 # (n, k): qkv, o / xq / xo, fc1, fc2, logits of tiny (d 384) and large-v3 (d 1280); then ragged and short shapes
 SHAPES = [(1152, 384), (384, 384), (1536, 384), (384, 1536), (51865, 384),
           (3840, 1280), (1280, 1280), (5120, 1280), (1280, 5120), (51866, 1280),
-          (37, 264), (33, 8), (100, 2056)]
+          (37, 264), (33, 8), (100, 2056), (40, 16384)]
 
 
 def _ref_geometry(m):
@@ -50,8 +50,18 @@ def dropin(cuda):
     return O.RefKernels(m.DROPIN_FATBIN)
 
 
+@pytest.fixture(params=["ring", "rows"])
+def form(request, monkeypatch):
+    """The library's two forms: the shared-memory ring (every Whisper shape) and the register-streaming form that
+    it falls back to when x and two 256-value stages per warp do not fit a CTA's shared memory (m k > 99 328:
+    (40, 16384) at m >= 7 takes it without the hook)."""
+    if request.param == "rows":
+        monkeypatch.setenv("MMZ_TEST_GEMV_ROWS", "1")
+    return request.param
+
+
 @pytest.mark.parametrize("n,k", SHAPES)
-def test_gemv_matches_reference(cuda, ref, n, k):
+def test_gemv_matches_reference(cuda, ref, form, n, k):
     import mimizuku_b200 as mm
     torch = cuda
     W, B = _weights(torch, n, k, n * 10 + k)
@@ -68,7 +78,7 @@ def test_gemv_matches_reference(cuda, ref, n, k):
 
 
 @pytest.mark.parametrize("m", [1, 3, 8])
-def test_gemv_padded_rows_and_no_bias(cuda, ref, m):
+def test_gemv_padded_rows_and_no_bias(cuda, ref, form, m):
     """x rows wider than k, y rows wider than n (the engine's [sequence][3d] buffers), no bias: the padding of y is
     left alone."""
     import mimizuku_b200 as mm
