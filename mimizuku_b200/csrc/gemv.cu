@@ -55,29 +55,6 @@ inline Plan plan(int m, int k) {
 }
 }  // namespace gq
 
-__host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
-
-// the values of lane l after the halving reduction of nv = COLS * MR values (index c * MR + m): lane l holds the full
-// sum of value (l >> (5 - log2 nv)) when nv <= 32
-template <int NV>
-__device__ __forceinline__ float halving_reduce(float (&v)[NV], int lane) {
-    static_assert(NV >= 1 && NV <= 32 && (NV & (NV - 1)) == 0, "power of two up to 32");
-    int o = 16;
-#pragma unroll
-    for (int half = NV / 2; half >= 1; half /= 2, o >>= 1) {
-        const bool up = lane & o;
-#pragma unroll
-        for (int j = 0; j < half; j++) {
-            const float send = up ? v[j] : v[j + half];
-            const float keep = up ? v[j + half] : v[j];
-            v[j] = keep + __shfl_xor_sync(0xffffffff, send, o);
-        }
-    }
-    float r = v[0];
-    for (; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffff, r, o);
-    return r;
-}
-
 // kc: the K chunk of a stage (a multiple of 256), stages: ring stages per warp (Plan)
 template <int MR>
 __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict__ x, int ldx,
@@ -148,56 +125,10 @@ __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict
             for (int kl = 8 * lane; kl < len; kl += 256) {  // this lane's groups of the chunk, in order
                 float w[COLS][8];
 #pragma unroll
-                for (int c = 0; c < COLS; c++) {
-                    const uint4 u = *reinterpret_cast<const uint4*>(st + c * len + kl);
-                    const __half2* p = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const float2 f2 = __half22float2(p[j]);
-                        w[c][2 * j] = f2.x;
-                        w[c][2 * j + 1] = f2.y;
-                    }
-                }
-                if constexpr (MR == 1) {
-                    const uint4 u = *reinterpret_cast<const uint4*>(xs + k0 + kl);
-                    const __half2* p = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const float2 f2 = __half22float2(p[j]);
-#pragma unroll
-                        for (int c = 0; c < COLS; c++) {
-                            acc[c][0] = __fmaf_rn(w[c][2 * j], f2.x, acc[c][0]);
-                            acc[c][0] = __fmaf_rn(w[c][2 * j + 1], f2.y, acc[c][0]);
-                        }
-                    }
-                } else {
-#pragma unroll
-                    for (int mp = 0; mp < MR / 2; mp++) {
-                        if (2 * mp < M) {
-                            const uint4 u0 = *reinterpret_cast<const uint4*>(xs + (2 * mp) * K + k0 + kl);
-                            const uint4 u1 = 2 * mp + 1 < M
-                                                 ? *reinterpret_cast<const uint4*>(xs + (2 * mp + 1) * K + k0 + kl)
-                                                 : make_uint4(0, 0, 0, 0);
-                            const __half2* p0 = reinterpret_cast<const __half2*>(&u0);
-                            const __half2* p1 = reinterpret_cast<const __half2*>(&u1);
-                            float2 xp[8];
-#pragma unroll
-                            for (int j = 0; j < 4; j++) {
-                                const float2 a = __half22float2(p0[j]), b = __half22float2(p1[j]);
-                                xp[2 * j] = make_float2(a.x, b.x);
-                                xp[2 * j + 1] = make_float2(a.y, b.y);
-                            }
-#pragma unroll
-                            for (int c = 0; c < COLS; c++) {
-                                float2 a2 = make_float2(acc[c][2 * mp], acc[c][2 * mp + 1]);
-#pragma unroll
-                                for (int j = 0; j < 8; j++) a2 = ffma2(make_float2(w[c][j], w[c][j]), xp[j], a2);
-                                acc[c][2 * mp] = a2.x;
-                                acc[c][2 * mp + 1] = a2.y;
-                            }
-                        }
-                    }
-                }
+                for (int c = 0; c < COLS; c++) halves8(*reinterpret_cast<const uint4*>(st + c * len + kl), w[c]);
+                const h16* xk = xs + k0 + kl;
+                gemv_group<MR, COLS>(
+                    w, [&](int m) { return *reinterpret_cast<const uint4*>(xk + m * K); }, M, acc);
             }
             __syncwarp();
             if (lane == 0 && v + stages < nunits) {
@@ -206,17 +137,7 @@ __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict
             }
         }
         if (!ok) break;
-        float vals[COLS * MR];
-#pragma unroll
-        for (int c = 0; c < COLS; c++)
-#pragma unroll
-            for (int m = 0; m < MR; m++) vals[c * MR + m] = acc[c][m];
-        const float r = halving_reduce<COLS * MR>(vals, lane);
-        constexpr int LOGV = ilog2(COLS * MR);
-        const int idx = lane >> (5 - LOGV), c = idx / MR, m = idx % MR;
-        const int n = (gw + t * nw) * COLS + c;
-        const bool lead = (lane & ((32 / (COLS * MR)) - 1)) == 0;  // one lane per value
-        if (lead && m < M && n < N) y[(long)m * ldy + n] = h(bias ? r + f(bias[n]) : r);
+        gemv_store<MR, COLS>(acc, lane, (gw + t * nw) * COLS, y, ldy, M, N, bias);
     }
     if (!ok) {
         // copies this warp issued and has not consumed land before it leaves; bounded, whatever the abort flag says
@@ -234,11 +155,22 @@ __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict
     }
 }
 
-template <int MR>
-__global__ void __launch_bounds__(256) gemv_kernel(const h16* __restrict__ x, int ldx, const h16* __restrict__ W,
-                                                   h16* __restrict__ y, int ldy, int M, int N, int K,
-                                                   const h16* __restrict__ bias) {
-    gemv_rows<MR>(x, ldx, W, y, ldy, M, N, K, bias);
+// the register form; GB groups of loads in flight per lane, MINB CTAs per SM
+template <int MR, int GB, int MINB>
+__global__ void __launch_bounds__(256, MINB) gemv_kernel(const h16* __restrict__ x, int ldx,
+                                                         const h16* __restrict__ W, h16* __restrict__ y, int ldy, int M,
+                                                         int N, int K, const h16* __restrict__ bias) {
+    gemv_rows<MR, GB>(x, ldx, W, y, ldy, M, N, K, bias);
+}
+
+template <int GB, int MINB>
+static cudaError_t launch_rows(const h16* X, int ldx, const h16* W, h16* Y, int ldy, int m, int n, int k,
+                               const h16* B, cudaStream_t st) {
+    const dim3 grid((n + gv::WARPS * gv::COLS - 1) / (gv::WARPS * gv::COLS));
+    if (m == 1) return launch_pdl(gemv_kernel<1, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
+    if (m == 2) return launch_pdl(gemv_kernel<2, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
+    if (m <= 4) return launch_pdl(gemv_kernel<4, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
+    return launch_pdl(gemv_kernel<8, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
 }
 
 void init_gemv_attrs() {
@@ -261,8 +193,13 @@ int launch_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, 
     auto Y = (h16*)y;
     auto B = (const h16*)bias;
     cudaError_t e;
-    const char* t = getenv("MMZ_TEST_GEMV_ROWS");  // a test hook: MMZ_TEST_GEMV_ROWS=1 takes the register form
+    // a test hook: MMZ_TEST_GEMV_ROWS=1 takes the register form with 5 groups in flight and one CTA per SM
+    const char* t = getenv("MMZ_TEST_GEMV_ROWS");
     const bool rows_form = t && t[0] == '1';
+    // Short rows over a long vocabulary (the tiny models' logits, k <= 512) stream best in the register form with
+    // two CTAs per SM (measured: 9.3 us against 14.1 us in the ring at 51865 x 384, m = 1); everything else goes
+    // through the ring where it fits (every large-model shape: up to 3.6x the register form at m = 8).
+    if (k <= 512 && n >= 8192 && !rows_form) return check_pdl(launch_rows<2, 2>(X, ldx, W, Y, ldy, m, n, k, B, st), "gemv");
     const gq::Plan pl = gq::plan(m, k);
     if (pl.kc > 0 && !rows_form) {
         const int items = (n + gq::COLS - 1) / gq::COLS;
@@ -274,12 +211,7 @@ int launch_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, 
         else e = launch_pdl(gemv_ring_kernel<8>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, dc.status, dc.limit_ns);
         return check_pdl(e, "gemv");
     }
-    const dim3 grid((n + gv::WARPS * gv::COLS - 1) / (gv::WARPS * gv::COLS));
-    if (m == 1) e = launch_pdl(gemv_kernel<1>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    else if (m == 2) e = launch_pdl(gemv_kernel<2>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    else if (m <= 4) e = launch_pdl(gemv_kernel<4>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    else e = launch_pdl(gemv_kernel<8>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    return check_pdl(e, "gemv");
+    return check_pdl(launch_rows<gv::GB, 1>(X, ldx, W, Y, ldy, m, n, k, B, st), "gemv");
 }
 
 }  // namespace mmz

@@ -50,10 +50,11 @@ def dropin(cuda):
     return O.RefKernels(m.DROPIN_FATBIN)
 
 
-@pytest.fixture(params=["ring", "rows"])
+@pytest.fixture(params=["chosen", "rows"])
 def form(request, monkeypatch):
-    """The library's two forms: the shared-memory ring (every Whisper shape) and the register-streaming form that
-    it falls back to when x and two 256-value stages per warp do not fit a CTA's shared memory (m k > 99 328:
+    """The library's own choice (the shared-memory ring for every large-model shape, the register form with two
+    CTAs per SM for the tiny vocabulary's k = 384 rows) and the register form with one CTA per SM, which the library
+    falls back to when x and two 256-value stages per warp do not fit a CTA's shared memory (m k > 99 328:
     (40, 16384) at m >= 7 takes it without the hook)."""
     if request.param == "rows":
         monkeypatch.setenv("MMZ_TEST_GEMV_ROWS", "1")
