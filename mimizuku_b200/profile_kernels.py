@@ -4,9 +4,10 @@
     python -m mimizuku_b200.profile_kernels enc            encoder attention, large-v3, 8 clips x 20 heads
     python -m mimizuku_b200.profile_kernels cross          cross-attention, large-v3, batch 32, one layer
     python -m mimizuku_b200.profile_kernels self [p]       self-attention, large-v3, batch 32, position p (default 223)
-    python -m mimizuku_b200.profile_kernels step [n]       n decoding steps (default 4) of the large-v3 engine at batch
-                                                           32 from one captured graph, inside the NVTX range "steps"
-                                                           (ncu --nvtx --nvtx-include "steps/" captures only those)
+    python -m mimizuku_b200.profile_kernels step [n] [b]   n decoding steps (default 4) of the large-v3 engine at batch
+                                                           b (default 32) from one captured graph, inside the NVTX
+                                                           range "steps" (ncu --nvtx --nvtx-include "steps/" captures
+                                                           only those)
     python -m mimizuku_b200.profile_kernels logits         logits fused with the greedy choice, large-v3, batch 32
     python -m mimizuku_b200.profile_kernels ln             add_layernorm at the encoder's 12000 x 1280
     python -m mimizuku_b200.profile_kernels logmel         the GPU log-mel of 32 synthetic 30 s clips (128 mel bins)
@@ -15,6 +16,8 @@
                                                            NVTX range "encode" (after one untimed group)
     python -m mimizuku_b200.profile_kernels gemm [mode]    the encoder's qkv projection (12000 x 3840 x 1280) on the
                                                            tensor-core GEMM; mode 1: fc1 with GELU (12000 x 5120 x 1280)
+    python -m mimizuku_b200.profile_kernels gemv [m] [n k] the decoder's gemv at m sequences (default 8) over the
+                                                           large-v3 logits (51866 x 1280) or n x k
 """
 import sys
 
@@ -60,13 +63,14 @@ def main(argv):
     elif which == "step":
         import numpy as np
         n = int(argv[1]) if len(argv) > 1 else 4
+        b = int(argv[2]) if len(argv) > 2 else 32
         cfg = m.LARGE_V3
-        e = m.Engine(cfg, bmax=32, eg=8, device=0, seed=1234, suppress=[cfg.eos])
-        mel16 = torch.randn(32, cfg.n_mels, 3000, device="cuda").half()
-        for g0 in range(0, 32, 8):
-            e.encode(mel16[g0].data_ptr(), 8, g0)
-        e.reset(np.tile(np.array(cfg.prompt, np.int32), (32, 1)))
-        e.capture(32, len(cfg.prompt))
+        e = m.Engine(cfg, bmax=b, eg=8, device=0, seed=1234, suppress=[cfg.eos])
+        mel16 = torch.randn(b, cfg.n_mels, 3000, device="cuda").half()
+        for g0 in range(0, b, 8):
+            e.encode(mel16[g0].data_ptr(), min(8, b - g0), g0)
+        e.reset(np.tile(np.array(cfg.prompt, np.int32), (b, 1)))
+        e.capture(b, len(cfg.prompt))
         for _ in range(len(cfg.prompt) + 8):  # past the prompt, graph captured and warm
             e.replay()
         e.sync()
@@ -123,6 +127,14 @@ def main(argv):
         c = torch.empty(M, N, device="cuda", dtype=torch.float16)
         for _ in range(4):
             m.gemm_bias(a, w, b, c, mode=mode)
+    elif which == "gemv":
+        mm = int(argv[1]) if len(argv) > 1 else 8
+        N, K = (int(argv[2]), int(argv[3])) if len(argv) > 3 else (51866, 1280)
+        w = (torch.randn(N, K, device="cuda") * 0.02).half()
+        x = torch.randn(mm, K, device="cuda").half()
+        y = torch.empty(mm, N, device="cuda", dtype=torch.float16)
+        for _ in range(4):
+            m.gemv(x, w, None, y)
     elif which == "align":
         n, mt, na, np_, rows = 32, 448, 10, 4, 223
         align = torch.rand(n, mt, na, 1500, device="cuda").half()
