@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(128)
         for (int i = 0; i < SSTAGE && i < total; i++) issue(i);
     }
     griddep_wait();  // launched as a programmatic dependent of the qkv projection
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     const long qrow = (long)b * 3 * d;
     const long crow = ((long)b * maxT + p) * d + hh * HD;
     if (t < 8) {  // the cache row of position p, for every sequence (kernels/whisper.cu:310-317)
@@ -438,6 +439,7 @@ __global__ void __launch_bounds__(64) cross_combine_kernel(const float* __restri
     const int hh = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
     const int bh = b * (d / HD) + hh;
     griddep_wait();
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     if (done[b]) return;
     float acc = 0.f;
     for (int c = 0; c < XNCH; c++) acc += __ldcg(&part[((long)bh * XNCH + c) * HD + t]);

@@ -13,8 +13,9 @@
 //     31 shuffles for 32 sums instead of 160;
 //   - in the register form, a warp issues GB groups of weight loads for its 4 columns (16 bytes per lane, a whole
 //     512-byte row segment per warp instruction) before their arithmetic, the first ones before the wait for the
-//     kernel before (the weights do not depend on it), and reads x (at most 8 rows) through the read-only cache
-//     instead of staging it in shared memory behind block barriers.
+//     kernel before (the weights do not depend on it), and reads x (at most 8 rows, written by the kernel before)
+//     from L2 (ld.global.cg, not the non-coherent path: this kernel may be resident before x is written) instead of
+//     staging it in shared memory behind block barriers.
 // Register form: grid ceil(N / 32), block 256: warp w of block b owns the columns 32 b + 4 w .. + 3.
 #pragma once
 #include "common.cuh"
@@ -160,7 +161,7 @@ __device__ __forceinline__ void gemv_rows(const h16* __restrict__ x, int ldx, co
             for (int c = 0; c < COLS; c++) halves8(wb[g][c], w[c]);
             const int k = 256 * i + 8 * lane;
             gemv_group<MR, COLS>(
-                w, [&](int m) { return __ldg(reinterpret_cast<const uint4*>(x + (long)m * ldx + k)); }, M, acc);
+                w, [&](int m) { return __ldcg(reinterpret_cast<const uint4*>(x + (long)m * ldx + k)); }, M, acc);
         }
     }
     gemv_store<MR, COLS>(acc, lane, n0, y, ldy, M, N, bias);

@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(128, 8) ln_warp_kernel(__half2* x, const __hal
                                                       const __half2* bias, __half2* out, int rows, int n2,
                                                       float eps) {
     griddep_wait();  // launched as a programmatic dependent: x and d come from the kernel before
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     const long row = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int l = threadIdx.x & 31;
@@ -106,6 +107,7 @@ template <int KP, bool ADD>
 __global__ void __launch_bounds__(128, 8) ln_vec_kernel(__half2* x, const __half2* dd, const __half2* w,
                                                      const __half2* bias, __half2* out, int rows, int n2, float eps) {
     griddep_wait();  // launched as a programmatic dependent: x and d come from the kernel before
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     const long row = (long)blockIdx.x * 4 + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int l = threadIdx.x & 31;

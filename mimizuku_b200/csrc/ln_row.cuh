@@ -39,6 +39,7 @@ __device__ __forceinline__ void ln_block_row(__half2* x, const __half2* dd, cons
         hb[k] = i < n2 ? bias[i] : __float2half2_rn(0.f);
     }
     griddep_wait();  // launched as a programmatic dependent: x and d come from the kernel before
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     __half2* xr = x + row * n2;
     const __half2* dr = ADD ? dd + row * n2 : nullptr;
     __half2 hx[KP], hd[KP];

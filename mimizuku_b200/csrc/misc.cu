@@ -13,6 +13,7 @@ static inline unsigned blocks(long n, int per) { return (unsigned)((n + per - 1)
 __global__ void embed_kernel(const int* __restrict__ tok, const int* __restrict__ ctr, const h16* __restrict__ emb,
                              const h16* __restrict__ pe, h16* __restrict__ x, int maxT, int d) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     const int b = blockIdx.x, p = ctr[0], t = tok[b * maxT + p];
     for (int c = threadIdx.x; c < d / 2; c += blockDim.x) {
         float2 e = __half22float2(reinterpret_cast<const __half2*>(emb + (long)t * d)[c]);
@@ -35,6 +36,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const h16* __restrict__ lo
                                                       int* tok, int* done, const int* ctr, int maxT, int prompt_len,
                                                       int eos, int bs1, int bs2) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     __shared__ float sv[32];
     __shared__ int si[32];
     const int b = blockIdx.x, p = ctr[0];
@@ -97,7 +99,11 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const h16* __restrict__ lo
     }
 }
 
-__global__ void advance_kernel(int* ctr) { griddep_wait(); ctr[0] += 1; }
+__global__ void advance_kernel(int* ctr) {
+    griddep_wait();
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
+    ctr[0] += 1;
+}
 
 // conv1 as a GEMM operand: X[g, t, ci * 3 + k] = mel[g, ci, t + k - 1] (kernels/whisper.cu:121-129)
 __global__ void im2col1_kernel(const h16* __restrict__ mel, h16* __restrict__ X, long n, int nm) {
@@ -184,6 +190,7 @@ __global__ void im2col2_vec_kernel(const h16* __restrict__ h1, h16* __restrict__
 __device__ __forceinline__ float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 __global__ void gelu_kernel(__half2* x, long n2) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n2) return;
     const float2 v = __half22float2(x[i]);
@@ -192,6 +199,7 @@ __global__ void gelu_kernel(__half2* x, long n2) {
 // the same, 8 values per 16-byte access (n a multiple of 8, x 16-byte aligned)
 __global__ void gelu8_kernel(uint4* x, long n8) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
+    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n8) return;
     uint4 u = x[i];
