@@ -69,30 +69,43 @@ __device__ __forceinline__ void gemv_group(const float (&w)[COLS][8], XRow xr, i
             }
         }
     } else {
+        // every row pair's x first, then the products with j outermost, so that the COLS x MR / 2 accumulator pairs
+        // form independent chains side by side (each still takes its 8 elements in order); rows m >= M read as zero
+        float2 xp[MR / 2][8];
 #pragma unroll
         for (int mp = 0; mp < MR / 2; mp++) {
-            if (2 * mp < M) {
-                const uint4 u0 = xr(2 * mp);
-                const uint4 u1 = 2 * mp + 1 < M ? xr(2 * mp + 1) : make_uint4(0, 0, 0, 0);
-                const __half2* p0 = reinterpret_cast<const __half2*>(&u0);
-                const __half2* p1 = reinterpret_cast<const __half2*>(&u1);
-                float2 xp[8];
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            const uint4 u0 = 2 * mp < M ? xr(2 * mp) : z;
+            const uint4 u1 = 2 * mp + 1 < M ? xr(2 * mp + 1) : z;
+            const __half2* p0 = reinterpret_cast<const __half2*>(&u0);
+            const __half2* p1 = reinterpret_cast<const __half2*>(&u1);
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const float2 a = __half22float2(p0[j]), b = __half22float2(p1[j]);
-                    xp[2 * j] = make_float2(a.x, b.x);
-                    xp[2 * j + 1] = make_float2(a.y, b.y);
-                }
-#pragma unroll
-                for (int c = 0; c < COLS; c++) {
-                    float2 a2 = make_float2(acc[c][2 * mp], acc[c][2 * mp + 1]);
-#pragma unroll
-                    for (int j = 0; j < 8; j++) a2 = ffma2(make_float2(w[c][j], w[c][j]), xp[j], a2);
-                    acc[c][2 * mp] = a2.x;
-                    acc[c][2 * mp + 1] = a2.y;
-                }
+            for (int j = 0; j < 4; j++) {
+                const float2 a = __half22float2(p0[j]), b = __half22float2(p1[j]);
+                xp[mp][2 * j] = make_float2(a.x, b.x);
+                xp[mp][2 * j + 1] = make_float2(a.y, b.y);
             }
         }
+        float2 a2[COLS][MR / 2];
+#pragma unroll
+        for (int c = 0; c < COLS; c++)
+#pragma unroll
+            for (int mp = 0; mp < MR / 2; mp++) a2[c][mp] = make_float2(acc[c][2 * mp], acc[c][2 * mp + 1]);
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+            for (int c = 0; c < COLS; c++) {
+                const float2 wd = make_float2(w[c][j], w[c][j]);
+#pragma unroll
+                for (int mp = 0; mp < MR / 2; mp++) a2[c][mp] = ffma2(wd, xp[mp][j], a2[c][mp]);
+            }
+#pragma unroll
+        for (int c = 0; c < COLS; c++)
+#pragma unroll
+            for (int mp = 0; mp < MR / 2; mp++) {
+                acc[c][2 * mp] = a2[c][mp].x;
+                acc[c][2 * mp + 1] = a2[c][mp].y;
+            }
     }
 }
 
