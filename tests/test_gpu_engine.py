@@ -111,13 +111,13 @@ def test_engine_lockstep_against_reference_kernels(cuda, ref):
     refe.close()
 
 
-@pytest.mark.parametrize("b", [9, 5])
+@pytest.mark.parametrize("b", [9, 5, 1])
 def test_decoder_and_timestamps_against_reference_kernels(cuda, ref, b):
     """Both engines decode from the same encoder output (the reference engine's cross k/v copied into the native
     one): the decoder path alone then gives the same tokens, nearly bit-identical alignment probabilities, and token
     timestamps (median filter + DTW) identical wherever the tokens agree. Nine sequences run every decoder GEMM
-    through cuBLAS in both engines; five run them, and the logits, through the gemv kernels (the reference's up to
-    8 rows, src/gpu.rs:211-228, this library's own in the native engine)."""
+    through cuBLAS in both engines; five and one run them, and the logits, through the gemv kernels (the reference's
+    up to 8 rows, src/gpu.rs:211-228, this library's own in the native engine)."""
     import mimizuku_b200 as m
     torch = cuda
     cfg = m.TINY

@@ -144,3 +144,32 @@ def test_large_decoder_and_timestamps_against_reference_kernels(cuda, ref, name,
     assert same_times == B, (same_times, moved)
     nat.close()
     refe.close()
+
+
+def test_large_small_batch_decoder_matches_reference_kernels(cuda, ref):
+    """Four sequences of large-v3: every decoder linear layer and the logits go through the gemv kernels (the
+    reference's up to 8 rows, src/gpu.rs:211-228; this library's ring-buffered gemv in the native engine, at k = 1280
+    and 5120). With the reference engine's cross k/v copied in, the two engines decode the same tokens and give every
+    clip the same token timestamps (tokens differing at most once, at a near-tie)."""
+    import mimizuku_b200 as m
+    torch = cuda
+    cfg = m.LARGE_V3
+    b, steps = 4, 24
+    mel, frames = _bench_clips(cfg.n_mels)
+    nat = m.Engine(cfg, bmax=b, eg=b, seed=SEED, suppress=[cfg.eos])
+    refe = m.Engine(cfg, bmax=b, eg=b, seed=SEED, suppress=[cfg.eos], kernel_image=O.REF_FATBIN)
+    mel16 = torch.from_numpy(mel[:b].astype(np.float16)).cuda()
+    refe.encode(mel16.data_ptr(), b, 0)
+    refe.sync()
+    O.d2d(nat.buffer("xkv"), refe.buffer("xkv"), 2 * b * cfg.dec_layers * 2 * cfg.d * 1500)
+    diverged, compared = _lockstep(cfg, nat, refe, b, steps)
+    np_ = len(cfg.prompt)
+    rows = steps - 1
+    for s in range(b):
+        wn, wr = _rows(nat, cfg, s, np_, rows), _rows(refe, cfg, s, np_, rows)
+        assert np.abs(wn - wr).max() < 2e-3
+        assert np.array_equal(m.jump_times(wn, frames[s] // 2), m.jump_times(wr, frames[s] // 2)), s
+    assert diverged <= 1, (diverged, compared)
+    assert m.status()[0] == 0
+    nat.close()
+    refe.close()
