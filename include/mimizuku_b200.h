@@ -130,6 +130,12 @@ int mmz_softmax_rows(void* s, long rows, int n, void* stream);
 int mmz_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
              void* stream);
 
+/* The decoder's fc1 product and the GELU after it (src/model.rs:708-709: Gpu::gemm of fc1, then gelu_inplace over
+ * its b x ff values, kernels/whisper.cu:106-113) in one launch at 1 <= m <= 8: mmz_gemv's rounded value, then
+ * rh(GELU) of it, equal bit for bit to the two reference kernels. Arguments and rules as mmz_gemv. */
+int mmz_gemv_gelu(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+                  void* stream);
+
 /* The encoder front end's data movement, with the reference kernels' arguments (kernels/whisper.cu:115-139, launched
  * at src/model.rs:553-559): im2col1 writes conv1's operand X[g][t][ci * 3 + k] = mel[g][ci][t + k - 1] (zero outside
  * the 3000 frames) for the n = groups x 3000 x 3 nm values; im2col2 writes conv2's X[g][t][ci * 3 + k] =

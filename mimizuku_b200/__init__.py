@@ -71,6 +71,7 @@ SIGNATURES = {
     "mmz_dec_linear": (_I, [_P, _I, _P, _P, _P, _I, _I, _I, _I, _I, _P]),
     "mmz_softmax_rows": (_I, [_P, _L, _I, _P]),
     "mmz_gemv": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _P]),
+    "mmz_gemv_gelu": (_I, [_P, _I, _P, _P, _I, _I, _I, _I, _P, _P]),
     "mmz_im2col1": (_I, [_P, _P, _LL, _I, _P]),
     "mmz_im2col2": (_I, [_P, _P, _LL, _I, _P]),
     "mmz_add_pos": (_I, [_P, _P, _LL, _I, _I, _P]),
@@ -276,13 +277,13 @@ def softmax_rows(s, n=None, rows=None, stream=None):
     _check(lib.mmz_softmax_rows(_ptr(s), rows, n, _stream(stream)), "softmax_rows")
 
 
-def gemv(x, w, bias, y, m=None, stream=None):
+def gemv(x, w, bias, y, m=None, gelu=False, stream=None):
     """y[m][n] = rh(x[m] . w[n] + bias[n]) for m <= 8 rows, bit-identical to the reference's gemv kernels; x [m][k],
-    w [n][k], y [m][n] fp16 device tensors, bias [n] or None."""
+    w [n][k], y [m][n] fp16 device tensors, bias [n] or None; gelu: then rh(GELU(y)), as gelu_inplace after it."""
     mm = m if m is not None else x.shape[0]
     n, k = w.shape
-    _check(lib.mmz_gemv(_ptr(x), x.stride(0), _ptr(w), _ptr(y), y.stride(0), mm, n, k, _ptr(bias), _stream(stream)),
-           "gemv")
+    fn = lib.mmz_gemv_gelu if gelu else lib.mmz_gemv
+    _check(fn(_ptr(x), x.stride(0), _ptr(w), _ptr(y), y.stride(0), mm, n, k, _ptr(bias), _stream(stream)), "gemv")
 
 
 def im2col1(mel, X, nm, n=None, stream=None):

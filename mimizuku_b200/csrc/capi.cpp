@@ -110,7 +110,11 @@ int mmz_softmax_rows(void* s, long rows, int n, void* stream) { return launch_so
 
 int mmz_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
              void* stream) {
-    return launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, S(stream));
+    return launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, false, S(stream));
+}
+int mmz_gemv_gelu(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+                  void* stream) {
+    return launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, true, S(stream));
 }
 int mmz_im2col1(const void* mel, void* X, long long n, int nm, void* stream) {
     if (n < 0 || nm < 1) return fail("im2col1: bad shape");

@@ -29,6 +29,8 @@ __device__ __forceinline__ void report(unsigned* status, unsigned code, unsigned
 __device__ __forceinline__ float f(h16 x) { return __half2float(x); }
 __device__ __forceinline__ h16 h(float x) { return __float2half_rn(x); }
 __device__ __forceinline__ float rh(float x) { return __half2float(__float2half_rn(x)); }
+// exact (erf) GELU of an fp16 value read as fp32 (kernels/whisper.cu:106-113: the decoder's and encoder's gelu_inplace)
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

@@ -58,6 +58,10 @@ class Kernels {
     // y = x W^T + bias for m <= 8 rows, or -2 when the image has no such kernel
     virtual int gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
                      cudaStream_t st) = 0;
+    // the same followed by gelu_inplace's GELU, in one kernel, or -2 when the image has none
+    virtual int gemv_gelu(const void*, int, const void*, void*, int, int, int, int, const void*, cudaStream_t) {
+        return -2;
+    }
     // the logits product hb emb^T (model.rs:714-716) where the image has a kernel for it; -2: use cuBLAS
     virtual int logits(const void*, int, const void*, void*, int, int, int, cudaStream_t) { return -2; }
     // the logits product, argmax_tok and advance as one kernel (model.rs:714-735) where the image has one; -2: no
@@ -130,7 +134,11 @@ class NativeKernels : public Kernels {
     }
     int gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
              cudaStream_t st) override {
-        return ++launches, launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, st);
+        return ++launches, launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, false, st);
+    }
+    int gemv_gelu(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
+                  cudaStream_t st) override {
+        return ++launches, launch_gemv(x, ldx, w, y, ldy, m, n, k, bias, true, st);
     }
     // split-K tensor-core product streaming the 133 MB embedding (8 < m <= 32; up to 8 sequences the reference's host
     // takes its gemv kernels, gpu.rs:211-228, and so does this engine, for the same logits bit for bit)
@@ -887,8 +895,13 @@ int Engine::dec_layer(int i, int r0, int bh, cudaStream_t st, cublasHandle_t h) 
     CK(k_->cross_attn(oxq, xkv, xs, stat_, part_, att, align, aslot_, ctr_, done, bh, i, nl, d, nh, na, mt, st));
     CK(lin_onto_bias_on(att, d, l.xo, oxo, d, bh, d, d, st, h));
     CK(k_->add_layernorm(x, oxo, l.ln3, hb, bh, d, st));
-    CK(lin_onto_bias_on(hb, d, l.fc1, ofc1, ff, bh, ff, d, st, h));
-    CK(k_->gelu(ofc1, (long)bh * ff, st));
+    // up to 8 sequences the fc1 product and its GELU are one kernel where the image has it (model.rs:708-709)
+    const int fg = bh <= 8 ? k_->gemv_gelu(hb, d, l.fc1.w, ofc1, ff, bh, ff, d, l.fc1.b, st) : -2;
+    if (fg == -1) return -1;
+    if (fg == -2) {
+        CK(lin_onto_bias_on(hb, d, l.fc1, ofc1, ff, bh, ff, d, st, h));
+        CK(k_->gelu(ofc1, (long)bh * ff, st));
+    }
     CK(lin_onto_bias_on(ofc1, ff, l.fc2, ofc2, d, bh, d, ff, st, h));
     const Ln& next = i + 1 < nl ? dec_[i + 1].ln1 : dln_;
     return k_->add_layernorm(x, ofc2, next, hb, bh, d, st);

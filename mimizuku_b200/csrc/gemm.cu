@@ -47,8 +47,6 @@ struct Smem {
     int abort;
 };
 
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
-
 }  // namespace gm
 
 using namespace gm;

@@ -60,7 +60,8 @@ template <int MR>
 __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict__ x, int ldx,
                                                            const h16* __restrict__ W, h16* __restrict__ y, int ldy,
                                                            int M, int N, int K, const h16* __restrict__ bias, int kc,
-                                                           int stages, unsigned* status, unsigned long long limit_ns) {
+                                                           int stages, int gelu, unsigned* status,
+                                                           unsigned long long limit_ns) {
     using namespace gq;
     extern __shared__ __align__(1024) unsigned char sm[];
     uint64_t* full = reinterpret_cast<uint64_t*>(sm);  // [WARPS][stages]
@@ -137,7 +138,7 @@ __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict
             }
         }
         if (!ok) break;
-        gemv_store<MR, COLS>(acc, lane, (gw + t * nw) * COLS, y, ldy, M, N, bias);
+        gemv_store<MR, COLS>(acc, lane, (gw + t * nw) * COLS, y, ldy, M, N, bias, gelu != 0);
     }
     if (!ok) {
         // copies this warp issued and has not consumed land before it leaves; bounded, whatever the abort flag says
@@ -159,18 +160,18 @@ __global__ void __launch_bounds__(256, 1) gemv_ring_kernel(const h16* __restrict
 template <int MR, int GB, int MINB>
 __global__ void __launch_bounds__(256, MINB) gemv_kernel(const h16* __restrict__ x, int ldx,
                                                          const h16* __restrict__ W, h16* __restrict__ y, int ldy, int M,
-                                                         int N, int K, const h16* __restrict__ bias) {
-    gemv_rows<MR, GB>(x, ldx, W, y, ldy, M, N, K, bias);
+                                                         int N, int K, const h16* __restrict__ bias, int gelu) {
+    gemv_rows<MR, GB>(x, ldx, W, y, ldy, M, N, K, bias, gelu != 0);
 }
 
 template <int GB, int MINB>
 static cudaError_t launch_rows(const h16* X, int ldx, const h16* W, h16* Y, int ldy, int m, int n, int k,
-                               const h16* B, cudaStream_t st) {
+                               const h16* B, int gelu, cudaStream_t st) {
     const dim3 grid((n + gv::WARPS * gv::COLS - 1) / (gv::WARPS * gv::COLS));
-    if (m == 1) return launch_pdl(gemv_kernel<1, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    if (m == 2) return launch_pdl(gemv_kernel<2, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    if (m <= 4) return launch_pdl(gemv_kernel<4, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
-    return launch_pdl(gemv_kernel<8, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B);
+    if (m == 1) return launch_pdl(gemv_kernel<1, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B, gelu);
+    if (m == 2) return launch_pdl(gemv_kernel<2, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B, gelu);
+    if (m <= 4) return launch_pdl(gemv_kernel<4, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B, gelu);
+    return launch_pdl(gemv_kernel<8, GB, MINB>, grid, dim3(256), 0, st, X, ldx, W, Y, ldy, m, n, k, B, gelu);
 }
 
 void init_gemv_attrs() {
@@ -181,7 +182,7 @@ void init_gemv_attrs() {
 }
 
 int launch_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
-                cudaStream_t st) {
+                bool gelu, cudaStream_t st) {
     if (m < 1 || m > 8 || n < 1 || k < 8 || k % 8 || ldx < k || ldy < n)
         return fail("gemv: 1 <= m <= 8, k a multiple of 8, ldx >= k, ldy >= n");
     if (((uintptr_t)x & 15) || ((uintptr_t)w & 15) || ((long)ldx * 2) % 16)
@@ -192,6 +193,7 @@ int launch_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, 
     auto W = (const h16*)w;
     auto Y = (h16*)y;
     auto B = (const h16*)bias;
+    const int g = gelu ? 1 : 0;
     cudaError_t e;
     // a test hook: MMZ_TEST_GEMV_ROWS=1 takes the register form with 5 groups in flight and one CTA per SM
     const char* t = getenv("MMZ_TEST_GEMV_ROWS");
@@ -199,19 +201,19 @@ int launch_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, 
     // Short rows over a long vocabulary (the tiny models' logits, k <= 512) stream best in the register form with
     // two CTAs per SM (measured: 9.3 us against 14.1 us in the ring at 51865 x 384, m = 1); everything else goes
     // through the ring where it fits (every large-model shape: up to 3.6x the register form at m = 8).
-    if (k <= 512 && n >= 8192 && !rows_form) return check_pdl(launch_rows<2, 2>(X, ldx, W, Y, ldy, m, n, k, B, st), "gemv");
+    if (k <= 512 && n >= 8192 && !rows_form) return check_pdl(launch_rows<2, 2>(X, ldx, W, Y, ldy, m, n, k, B, g, st), "gemv");
     const gq::Plan pl = gq::plan(m, k);
     if (pl.kc > 0 && !rows_form) {
         const int items = (n + gq::COLS - 1) / gq::COLS;
         const dim3 grid(items < dc.sms ? items : dc.sms);
         const int kc = pl.kc, ns = pl.stages;
-        if (m == 1) e = launch_pdl(gemv_ring_kernel<1>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, dc.status, dc.limit_ns);
-        else if (m == 2) e = launch_pdl(gemv_ring_kernel<2>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, dc.status, dc.limit_ns);
-        else if (m <= 4) e = launch_pdl(gemv_ring_kernel<4>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, dc.status, dc.limit_ns);
-        else e = launch_pdl(gemv_ring_kernel<8>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, dc.status, dc.limit_ns);
+        if (m == 1) e = launch_pdl(gemv_ring_kernel<1>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, g, dc.status, dc.limit_ns);
+        else if (m == 2) e = launch_pdl(gemv_ring_kernel<2>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, g, dc.status, dc.limit_ns);
+        else if (m <= 4) e = launch_pdl(gemv_ring_kernel<4>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, g, dc.status, dc.limit_ns);
+        else e = launch_pdl(gemv_ring_kernel<8>, grid, dim3(256), pl.smem, st, X, ldx, W, Y, ldy, m, n, k, B, kc, ns, g, dc.status, dc.limit_ns);
         return check_pdl(e, "gemv");
     }
-    return check_pdl(launch_rows<gv::GB, 1>(X, ldx, W, Y, ldy, m, n, k, B, st), "gemv");
+    return check_pdl(launch_rows<gv::GB, 1>(X, ldx, W, Y, ldy, m, n, k, B, g, st), "gemv");
 }
 
 }  // namespace mmz

@@ -120,10 +120,12 @@ __device__ __forceinline__ void halves8(const uint4& u, float (&o)[8]) {
     }
 }
 
-// the lane reduction of a warp's COLS x MR sums and their store: columns n0 .. n0 + COLS - 1, rows m < M
+// the lane reduction of a warp's COLS x MR sums and their store: columns n0 .. n0 + COLS - 1, rows m < M; gelu: the
+// rounded value then goes through gelu_inplace's GELU and is rounded again (the fc1 product and the GELU after it,
+// model.rs:708-709, in one kernel)
 template <int MR, int COLS>
 __device__ __forceinline__ void gemv_store(const float (&acc)[COLS][MR], int lane, int n0, h16* __restrict__ y,
-                                           int ldy, int M, int N, const h16* __restrict__ bias) {
+                                           int ldy, int M, int N, const h16* __restrict__ bias, bool gelu = false) {
     float vals[COLS * MR];
 #pragma unroll
     for (int c = 0; c < COLS; c++)
@@ -133,13 +135,17 @@ __device__ __forceinline__ void gemv_store(const float (&acc)[COLS][MR], int lan
     constexpr int LOGV = ilog2(COLS * MR);
     const int idx = lane >> (5 - LOGV), c = idx / MR, m = idx % MR;
     const bool lead = (lane & ((32 / (COLS * MR)) - 1)) == 0;  // one lane per value
-    if (lead && m < M && n0 + c < N) y[(long)m * ldy + n0 + c] = h(bias ? r + f(bias[n0 + c]) : r);
+    if (lead && m < M && n0 + c < N) {
+        h16 v = h(bias ? r + f(bias[n0 + c]) : r);
+        if (gelu) v = h(gelu_erf(f(v)));
+        y[(long)m * ldy + n0 + c] = v;
+    }
 }
 
 template <int MR, int GB = gv::GB>
 __device__ __forceinline__ void gemv_rows(const h16* __restrict__ x, int ldx, const h16* __restrict__ W,
                                           h16* __restrict__ y, int ldy, int M, int N, int K,
-                                          const h16* __restrict__ bias) {
+                                          const h16* __restrict__ bias, bool gelu = false) {
     using namespace gv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = (blockIdx.x * WARPS + warp) * COLS;
@@ -177,7 +183,7 @@ __device__ __forceinline__ void gemv_rows(const h16* __restrict__ x, int ldx, co
                 w, [&](int m) { return __ldcg(reinterpret_cast<const uint4*>(x + (long)m * ldx + k)); }, M, acc);
         }
     }
-    gemv_store<MR, COLS>(acc, lane, n0, y, ldy, M, N, bias);
+    gemv_store<MR, COLS>(acc, lane, n0, y, ldy, M, N, bias, gelu);
 }
 
 }  // namespace mmz

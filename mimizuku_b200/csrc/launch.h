@@ -116,9 +116,10 @@ int launch_argmax_tok(const void* logits, int V, const unsigned char* sup, int* 
 int launch_advance(int* ctr, cudaStream_t st);
 // row softmax in place, rows of n <= 2048 fp16 values (8-byte aligned rows): the unfused encoder attention's
 int launch_softmax_rows(void* s, long rows, int n, cudaStream_t st);
-// y[m][n] = rh(x[m] . W[n] + bias[n]) for m <= 8, bit-identical to the reference's gemv kernels (gemv.cu)
+// y[m][n] = rh(x[m] . W[n] + bias[n]) for m <= 8, bit-identical to the reference's gemv kernels (gemv.cu); gelu: then
+// rh(GELU(y)), as gelu_inplace after it
 int launch_gemv(const void* x, int ldx, const void* w, void* y, int ldy, int m, int n, int k, const void* bias,
-                cudaStream_t st);
+                bool gelu, cudaStream_t st);
 int launch_im2col1(const void* mel, void* X, long n, int nm, cudaStream_t st);
 int launch_im2col2(const void* h1, void* X, long n, int d, cudaStream_t st);
 int launch_gelu(void* x, long n, cudaStream_t st);

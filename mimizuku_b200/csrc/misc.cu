@@ -187,7 +187,7 @@ __global__ void im2col2_vec_kernel(const h16* __restrict__ h1, h16* __restrict__
 }
 
 // exact (erf) GELU over half2 pairs (kernels/whisper.cu:106-113)
-__device__ __forceinline__ float gelu(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu(float v) { return gelu_erf(v); }
 __global__ void gelu_kernel(__half2* x, long n2) {
     griddep_wait();  // launched as a programmatic dependent of the previous kernel
     griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)

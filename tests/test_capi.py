@@ -69,6 +69,7 @@ def test_kernel_entry_points_validate_shapes_before_touching_a_device():
     assert v(None, 16, None, None, 16, 1, 16, 12, None, None) != 0
     assert v(None, 8, None, None, 16, 1, 16, 16, None, None) != 0
     assert v(8, 16, 16, None, 16, 1, 16, 16, None, None) != 0  # x not 16-byte aligned
+    assert m.lib.mmz_gemv_gelu(None, 16, None, None, 16, 9, 16, 16, None, None) != 0
     assert m.lib.mmz_im2col1(None, None, 10, 0, None) != 0
     assert m.lib.mmz_add_pos(None, None, 4, 8, 0, None) != 0
 

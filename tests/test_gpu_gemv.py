@@ -113,3 +113,23 @@ def test_gemv_by_name_matches_reference(cuda, ref, dropin, n, k):
             outs.append(Y)
         torch.cuda.synchronize()
         assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16)), (m, n, k)
+
+
+@pytest.mark.parametrize("n,k", [(5120, 1280), (1536, 384), (1000, 264)])
+def test_gemv_gelu_matches_reference_gemv_then_gelu(cuda, ref, form, n, k):
+    """The decoder's fc1 product and its GELU in one launch (mmz_gemv_gelu) against the reference's gemv kernel
+    followed by its gelu_inplace over the b x ff values (src/model.rs:708-709): equal bit for bit."""
+    import mimizuku_b200 as mm
+    torch = cuda
+    W, B = _weights(torch, n, k, n + 3 * k)
+    for m in (1, 2, 3, 5, 8):
+        X = _rows(torch, m, k, 10 + m)
+        Y = torch.full((m, n), 7.0, dtype=torch.float16, device="cuda")
+        Yr = torch.full((m, n), 7.0, dtype=torch.float16, device="cuda")
+        mm.gemv(X, W, B, Y, gelu=True)
+        _launch_by_name(ref, m, n, k, X, k, W, Yr, n, B)
+        n2 = m * n // 2
+        ref.launch("gelu_inplace", ((n2 + 255) // 256,), 256, [("p", Yr.data_ptr()), ("l", n2)])
+        torch.cuda.synchronize()
+        assert mm.status()[0] == 0
+        assert torch.equal(Y.view(torch.int16), Yr.view(torch.int16)), (m, n, k)
