@@ -438,8 +438,7 @@ __global__ void __launch_bounds__(64) cross_combine_kernel(const float* __restri
                                                            const int* __restrict__ done, int d) {
     const int hh = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
     const int bh = b * (d / HD) + hh;
-    griddep_wait();
-    griddep_launch_dependents();  // this kernel has waited: the next one may be scheduled (it waits for this one)
+    griddep_wait();  // no early launch of the next kernel: back-to-back cross-attentions ran 50.1 us against 45.8
     if (done[b]) return;
     float acc = 0.f;
     for (int c = 0; c < XNCH; c++) acc += __ldcg(&part[((long)bh * XNCH + c) * HD + t]);
