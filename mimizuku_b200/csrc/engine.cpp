@@ -912,7 +912,10 @@ int Engine::step(int b, int prompt_len) {
     const int d = dm_.d, ff = dm_.ff, nl = dm_.dec_layers, mt = dm_.max_t;
     CK(k_->embed(tok_, ctr_, emb_, dpos_, x_, b, mt, d, st_));
     CK(k_->layernorm(x_, dec_[0].ln1, hb_, b, d, st_));
-    CUDA_CK(cudaMemcpyAsync(dout_, dbias_, (size_t)2 * nl * bmax_ * (7 * d + ff), cudaMemcpyDeviceToDevice, st_));
+    // the bias images the cuBLAS products accumulate onto; up to 8 sequences the native gemv adds the bias itself and
+    // overwrites every output, so the copy (and the break it makes in the chain of programmatic launches) is left out
+    if (!(b <= 8 && k_->native()))
+        CUDA_CK(cudaMemcpyAsync(dout_, dbias_, (size_t)2 * nl * bmax_ * (7 * d + ff), cudaMemcpyDeviceToDevice, st_));
     if (lanes_ == 2 && b == 2 * LANE_ROWS) {
         // two lanes: the first half of the sequences on the engine's stream, the second half on the other; forked
         // here, joined before the logits (also inside a graph capture, where the second stream joins the capture)
