@@ -445,6 +445,151 @@ __global__ void __launch_bounds__(64) cross_combine_kernel(const float* __restri
     out[(long)b * d + hh * HD + t] = h(acc);
 }
 
+// The three kernels above as one launch, for the decoding step at small batches, where the launches rather than the
+// bytes set its time: grid (8, heads, B) in clusters of the 8 CTAs of a (sequence, head), each with the same 192
+// positions as cross_scores_kernel and cross_pv_kernel. The scores stay in shared memory; each CTA sends its three
+// chunk statistics to every CTA of the cluster (distributed shared memory) and, after a cluster barrier, forms the
+// global max and sum from all 24 in chunk order, as cross_pv_kernel does from the scratch; the chunk partials of P.V go
+// to CTA 0 of the cluster, which sums them in chunk order after a second barrier, as cross_combine_kernel does. Every
+// value is formed by the same operations in the same order as in the three kernels, so the outputs and the alignment
+// probabilities are theirs bit for bit. K and V come from the encoder and ctr / done from earlier steps: all copies are
+// in flight before the wait for the kernel before (q comes from it). Every CTA of a cluster has the same sequence, so a
+// finished one leaves as a whole cluster, before either barrier.
+__global__ void __cluster_dims__(XCL, 1, 1) __launch_bounds__(128)
+    cross_fused_kernel(const h16* __restrict__ q, const h16* __restrict__ kv, h16* __restrict__ out,
+                       h16* __restrict__ align, const int* __restrict__ aslot, const int* __restrict__ ctr,
+                       const int* __restrict__ done, int layer, int nl, int d, int na, int maxT, unsigned* status,
+                       unsigned long long limit_ns) {
+    constexpr int PT = XPER / 16;  // positions per lane group of 8
+    __shared__ __align__(128) h16 vs[XPER * HD];  // this CTA's V slice, then the group partials
+    __shared__ float qs[HD];
+    __shared__ float sc[XPER];      // the rounded scores, then the probabilities
+    __shared__ float2 gs[XNCH];     // the 24 chunk statistics of the (sequence, head), from every CTA of the cluster
+    __shared__ float part[XNCH * HD];  // CTA 0: the 24 chunk partials of P.V
+    __shared__ float2 gms;
+    __shared__ uint64_t bar[XCPC];
+    __shared__ int abort;
+    static_assert(XCPC * 16 * HD * 4 <= XPER * HD * 2, "the group partials fit in the V slice");
+    const int b = blockIdx.z, hh = blockIdx.y, t = threadIdx.x;
+    const int r = (int)cluster_rank();
+    const int nh = d / HD;
+    if (done[b]) return;
+    cluster_arrive_relaxed();  // waited for before the first store into another CTA's shared memory
+    const int j0 = r * XPER, n = min(XPER, TENC - j0);
+    const int grp = t >> 3, sub = t & 7;
+    const h16* K = kv + xkv_off(b, layer, 0, hh, nl, nh) + (long)j0 * HD + sub * 8;
+    uint4 u[PT];
+#pragma unroll
+    for (int i = 0; i < PT; i++) {
+        const int jj = grp + 16 * i;
+        u[i] = jj < n ? ldg_stream(K + jj * HD) : make_uint4(0, 0, 0, 0);
+    }
+    if (t == 0) {
+        abort = 0;
+        const h16* V = kv + xkv_off(b, layer, 1, hh, nl, nh) + (long)j0 * HD;
+        for (int c = 0; c < XCPC; c++) mbar_init(&bar[c], 1);
+        fence_mbar_init();
+        for (int c = 0; c < XCPC; c++) {
+            const int nc = min(XCH, n - c * XCH);
+            mbar_expect_tx(&bar[c], nc * HD * 2);
+            bulk_g2s(vs + c * XCH * HD, V + (long)c * XCH * HD, nc * HD * 2, &bar[c]);
+        }
+    }
+    griddep_wait();  // q comes from the kernel before
+    griddep_launch_dependents();
+    if (t < HD) qs[t] = rh(f(q[(long)b * d + hh * HD + t]) * 0.125f);
+    __syncthreads();
+    // scores: a group of 8 lanes per position (kernels/whisper.cu:376-392)
+#pragma unroll
+    for (int i = 0; i < PT; i++) {
+        const int jj = grp + 16 * i;
+        const __half2* p2 = reinterpret_cast<const __half2*>(&u[i]);
+        float a = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            float2 v = __half22float2(p2[e]);
+            a += qs[sub * 8 + 2 * e] * v.x + qs[sub * 8 + 2 * e + 1] * v.y;
+        }
+        for (int o = 4; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffff, a, o);
+        if (sub == 0) sc[jj] = jj < n ? rh(a) : -INFINITY;
+    }
+    __syncthreads();
+    cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
+    // chunk statistics, warp c for chunk c (kernels/whisper.cu:394-401), sent to every CTA of the cluster
+    const int w = t >> 5, lane = t & 31;
+    if (w < XCPC) {
+        float a = sc[w * XCH + lane], b2 = sc[w * XCH + lane + 32];
+        float m = fmaxf(a, b2);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffff, m, o));
+        float sm = (a == -INFINITY ? 0.f : expf(a - m)) + (b2 == -INFINITY ? 0.f : expf(b2 - m));
+        for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffff, sm, o);
+        if (lane < XCL) st_dsmem_f32x2(dsmem_addr(&gs[r * XCPC + w], lane), make_float2(m, sm));
+    }
+    cluster_sync();  // every CTA holds the 24 statistics
+    // the global max and sum over the 24 chunks in order (kernels/whisper.cu:414-417), as in cross_pv_kernel
+    if (t < 32) {
+        const float2 g2 = t < XNCH ? gs[t] : make_float2(-INFINITY, 0.f);
+        float mx = g2.x;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, o));
+        const float e = t < XNCH ? expf(g2.x - mx) : 0.f;
+        float sm = 0.f;
+        for (int c = 0; c < XNCH; c++)
+            sm = __fmaf_rn(__shfl_sync(0xffffffff, g2.y, c), __shfl_sync(0xffffffff, e, c), sm);
+        if (t == 0) gms = make_float2(mx, sm);
+    }
+    __syncthreads();
+    const float m = gms.x, sum = gms.y;
+    const int slot = aslot[layer * nh + hh];
+    h16* arow = slot >= 0 ? align + (((long)b * maxT + ctr[0]) * na + slot) * TENC + j0 : nullptr;
+    for (int jj = t; jj < n; jj += 128) {
+        float pj = rh(expf(sc[jj] - m) / sum);
+        sc[jj] = pj;
+        if (arow) arow[jj] = h(pj);
+    }
+    __syncthreads();
+    // P.V per chunk (kernels/whisper.cu:421-438), as in cross_pv_kernel
+    float a[XCPC][8];
+#pragma unroll
+    for (int c = 0; c < XCPC; c++) {
+        mbar_wait_spin(&bar[c], 0, &abort, limit_ns, status, K_CROSS, 8 + c);
+        const int nc = min(XCH, n - c * XCH);
+#pragma unroll
+        for (int e = 0; e < 8; e++) a[c][e] = 0.f;
+        for (int jj = grp; jj < nc; jj += 16) {
+            const uint4 uv = *reinterpret_cast<const uint4*>(vs + (c * XCH + jj) * HD + sub * 8);
+            const __half2* p2 = reinterpret_cast<const __half2*>(&uv);
+            const float pj = sc[c * XCH + jj];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float2 v = __half22float2(p2[e]);
+                a[c][2 * e] += pj * v.x;
+                a[c][2 * e + 1] += pj * v.y;
+            }
+        }
+    }
+    __syncthreads();  // V is no longer read
+    float* red = reinterpret_cast<float*>(vs);  // [XCPC][16][HD]
+#pragma unroll
+    for (int c = 0; c < XCPC; c++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) red[(c * 16 + grp) * HD + sub * 8 + e] = a[c][e];
+    __syncthreads();
+    for (int i = t; i < XCPC * HD; i += 128) {
+        const int c = i / HD, col = i % HD;
+        float acc = 0.f;
+        for (int g = 0; g < 16; g++) acc += red[(c * 16 + g) * HD + col];
+        st_dsmem_f32(dsmem_addr(&part[(r * XCPC + c) * HD + col], 0), acc);
+    }
+    if (t == 0 && abort)
+        for (int c = 0; c < XCPC; c++) mbar_wait(&bar[c], 0, nullptr, limit_ns, nullptr, 0, 0);
+    cluster_sync();  // CTA 0 holds the 24 partials
+    if (r == 0 && t < HD) {  // the partials summed in chunk order (kernels/whisper.cu:443-449)
+        float acc = 0.f;
+        for (int c = 0; c < XNCH; c++) acc += part[c * HD + t];
+        out[(long)b * d + hh * HD + t] = h(acc);
+    }
+}
+
 // kernels/whisper.cu:310-317 as its own launch (the engine folds it into self_attn_kernel): k and v of position p
 // into the caches, 16-byte copies.
 __global__ void kv_write_kernel(const h16* __restrict__ qkv, h16* __restrict__ kc, h16* __restrict__ vc,
@@ -458,6 +603,19 @@ __global__ void kv_write_kernel(const h16* __restrict__ qkv, h16* __restrict__ k
 }
 
 // ============================================================================ launchers
+
+int launch_cross_fused(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
+                       const int* done, int batch, int layer, int nl, int d, int na, int maxT, cudaStream_t st) {
+    if (batch < 1 || batch > 65535 || d < HD || d % HD || layer < 0 || layer >= nl || maxT < 1 || na < 0)
+        return fail("cross_fused: bad shape");
+    if (((uintptr_t)kv & 15) || ((uintptr_t)q & 3)) return fail("cross_fused: kv must be 16-byte aligned");
+    DevCtx& dc = dev_ctx();
+    if (!dc.ok) return fail(dc.err);
+    return check_pdl(launch_pdl(cross_fused_kernel, dim3(XCL, d / HD, batch), dim3(128), 0, st, (const h16*)q,
+                                (const h16*)kv, (h16*)out, (h16*)align, aslot, ctr, done, layer, nl, d, na, maxT,
+                                dc.status, dc.limit_ns),
+                     "cross_fused");
+}
 
 size_t cross_attn_scratch_bytes(int batch, int d) { return cross_scratch_bytes(batch, d / HD); }
 

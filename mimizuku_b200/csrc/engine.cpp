@@ -100,6 +100,10 @@ class NativeKernels : public Kernels {
     int cross_attn(const void* xq, const void* kv, void* s, void*, void*, void* att, void* align, const int* aslot,
                    const int* ctr, const int* done, int b, int layer, int nl, int d, int, int na, int maxT,
                    cudaStream_t st) override {
+        if (b <= cross_fused_max) {  // small batches: the three kernels as one launch on clusters, no scratch
+            ++launches;
+            return launch_cross_fused(xq, kv, att, align, aslot, ctr, done, b, layer, nl, d, na, maxT, st);
+        }
         char* base = s ? (char*)s : (char*)xscratch;
         const size_t used = (size_t)(base - (char*)xscratch);
         if (used > xscratch_bytes) return fail("cross_attn: scratch offset out of range");
@@ -148,6 +152,9 @@ class NativeKernels : public Kernels {
     }
     // the logits streamed once and reduced to each sequence's token on the GPU, no [b][vocab] logits in memory
     // (8 < m <= 32, d <= 1280); lgscratch: its zero-initialised scratch, owned by the engine
+    // up to this many sequences the cross-attention is one launch (cross_fused_kernel); a test hook,
+    // MMZ_CROSS_FUSED_MAX=<n>, moves the limit (0: always the three kernels)
+    int cross_fused_max = 8;
     void* lgscratch = nullptr;
     size_t lgscratch_bytes = 0;
     bool fused_logits = true;
@@ -468,6 +475,7 @@ Engine::Engine(const Dims& dims, const GenCfg& gc, int bmax, int eg, const char*
         // a test hook: MMZ_TEST_UNFUSED_LOGITS=1 keeps the logits product, argmax_tok and advance as three launches, so
         // that the two paths can be compared
         if (const char* t = getenv("MMZ_TEST_UNFUSED_LOGITS")) nk->fused_logits = t[0] != '1';
+        if (const char* t = getenv("MMZ_CROSS_FUSED_MAX")) nk->cross_fused_max = atoi(t);
         s_ = nk->xscratch;
         stat_ = part_ = nullptr;
     }

@@ -69,6 +69,9 @@ void init_align_attrs();
 
 // launchers (device pointers, asynchronous on `st`); 0 on success, -1 with the last error set
 size_t cross_attn_scratch_bytes(int batch, int d);
+// launch_cross_attn's three kernels as one launch on clusters of 8 CTAs, no scratch (dec_attn.cu), bit-identical
+int launch_cross_fused(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
+                       const int* done, int batch, int layer, int nl, int d, int na, int maxT, cudaStream_t st);
 int launch_cross_attn(const void* q, const void* kv, void* out, void* align, const int* aslot, const int* ctr,
                       const int* done, int batch, int layer, int nl, int d, int na, int maxT, void* scratch,
                       size_t scratch_bytes, cudaStream_t st);

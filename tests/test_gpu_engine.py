@@ -296,3 +296,27 @@ def test_fused_logits_argmax_matches_three_launches(cuda, monkeypatch, b):
         for k in ("tokens", "lens", "times"):
             assert np.array_equal(out[key][k], out[True, True][k]), (key, k)
     assert (out[False, True]["lens"] == len(cfg.prompt) + 20).all()
+
+
+@pytest.mark.parametrize("b", [1, 5, 8])
+def test_one_launch_cross_attention_matches_three(cuda, monkeypatch, b):
+    """Up to 8 sequences the native step runs the cross-attention as one launch on clusters of 8 CTAs (no scratch);
+    its tokens, times and every alignment probability equal those of the three-kernel cross-attention (the library's
+    hook MMZ_CROSS_FUSED_MAX=0 keeps it), bit for bit."""
+    import mimizuku_b200 as m
+    cfg = m.TINY
+    mel, frames = _clips(b, cfg.n_mels, seed=17)
+    res = {}
+    for mx in ("8", "0"):
+        monkeypatch.setenv("MMZ_CROSS_FUSED_MAX", mx)
+        e = m.Engine(cfg, bmax=b, eg=min(b, 8), seed=6, suppress=[cfg.eos])
+        monkeypatch.delenv("MMZ_CROSS_FUSED_MAX", raising=False)
+        out = e.transcribe(mel, frames, max_new=20, graph=True)
+        al = np.empty(b * cfg.max_t * e.na * 1500, np.float16)
+        O.d2h(al, e.buffer("align"))
+        res[mx] = (out, al.view(np.uint16))
+        e.close()
+    for k in ("tokens", "lens", "times"):
+        assert np.array_equal(res["8"][0][k], res["0"][0][k]), k
+    assert np.array_equal(res["8"][1], res["0"][1])
+    assert m.status()[0] == 0
