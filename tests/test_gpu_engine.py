@@ -298,18 +298,21 @@ def test_fused_logits_argmax_matches_three_launches(cuda, monkeypatch, b):
     assert (out[False, True]["lens"] == len(cfg.prompt) + 20).all()
 
 
-@pytest.mark.parametrize("b", [1, 5, 8])
-def test_one_launch_cross_attention_matches_three(cuda, monkeypatch, b):
+@pytest.mark.parametrize("b,eos", [(1, False), (5, False), (8, False), (6, True)])
+def test_one_launch_cross_attention_matches_three(cuda, monkeypatch, b, eos):
     """Up to 8 sequences the native step runs the cross-attention as one launch on clusters of 8 CTAs (no scratch);
     its tokens, times and every alignment probability equal those of the three-kernel cross-attention (the library's
-    hook MMZ_CROSS_FUSED_MAX=0 keeps it), bit for bit."""
+    hook MMZ_CROSS_FUSED_MAX=0 keeps it), bit for bit; also when every sequence has finished and both skip it."""
     import mimizuku_b200 as m
     cfg = m.TINY
     mel, frames = _clips(b, cfg.n_mels, seed=17)
     res = {}
     for mx in ("8", "0"):
         monkeypatch.setenv("MMZ_CROSS_FUSED_MAX", mx)
-        e = m.Engine(cfg, bmax=b, eg=min(b, 8), seed=6, suppress=[cfg.eos])
+        # eos: only end-of-text left, so every sequence ends at its first token and the steps run until the next
+        # poll of the finished flags skip them all
+        sup = [t for t in range(cfg.vocab) if t != cfg.eos] if eos else [cfg.eos]
+        e = m.Engine(cfg, bmax=b, eg=min(b, 8), seed=6, suppress=sup)
         monkeypatch.delenv("MMZ_CROSS_FUSED_MAX", raising=False)
         out = e.transcribe(mel, frames, max_new=20, graph=True)
         al = np.empty(b * cfg.max_t * e.na * 1500, np.float16)
@@ -319,4 +322,6 @@ def test_one_launch_cross_attention_matches_three(cuda, monkeypatch, b):
     for k in ("tokens", "lens", "times"):
         assert np.array_equal(res["8"][0][k], res["0"][0][k]), k
     assert np.array_equal(res["8"][1], res["0"][1])
+    if eos:
+        assert (res["8"][0]["lens"] == len(cfg.prompt) + 1).all(), res["8"][0]["lens"]
     assert m.status()[0] == 0
